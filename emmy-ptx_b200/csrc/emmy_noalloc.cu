@@ -14,15 +14,26 @@
 // `<entry>_ksplit` pre-pass and the attention kernel) from the caller's
 // module, through libemmy_rt.
 //
+// Shape: the call refuses (ERT_E_ARGUMENT, before any copy or launch) a
+// heads_total/seq/head_dim that differs from the shape the module was
+// compiled for, which the module records in the name of a global
+// (emmy_attn_shape_<heads_total>x<seq>x<head_dim>).  The pre-pass writes the
+// compiled element count, so only a matching shape keeps it inside the array.
+//
 // Set-up: the first call on a device (with that device's context current)
-// resolves the array's address with cudaGetSymbolAddress and caches it; make
-// that first call before any stream capture begins.  Nothing in the scratch
+// resolves the array's address with cudaGetSymbolAddress and caches it; with
+// lazy module loading that is also when the library's device image, and with
+// it the array, is loaded onto the device.  Make that first call before any
+// stream capture begins.  Nothing in the scratch
 // has to start at zero: the pre-pass writes every byte the attention kernel
 // reads, and the tensor maps zero-fill rows past the sequence end.
 //
 // Calls share one scratch array and rewrite the module's three tensor-map
 // globals, so two calls that overlap in time (different streams, or threads
 // without ordering) race; issue them on one stream or order them on the host.
+// For the same reason a module used with this call must not also be launched
+// through emmy_ptx.runtime.Kernel: Kernel caches the tensor maps it wrote and
+// does not see that this call replaced them.
 
 #include <cuda_runtime.h>
 
@@ -138,6 +149,21 @@ extern "C" int ert_attention_noalloc(uint64_t module, uint64_t attention_fn, uin
     if ((k | v) & 15)
         return fail(err, err_len, ERT_E_ARGUMENT,
                     "ert_attention_noalloc: K and V must be 16-byte aligned");
+
+    // The pre-pass's element count and the kernel's loops are compiled into
+    // the module; the scratch check above holds only if the stated shape is
+    // that shape.  The module records it in the name of a global, so a host
+    // lookup (no device read, no synchronisation) settles it.
+    char shape_name[96];
+    snprintf(shape_name, sizeof shape_name, "emmy_attn_shape_%ux%ux%u", heads_total, seq,
+             head_dim);
+    uint64_t shape_ptr = 0;
+    if (ert_module_global(module, shape_name, &shape_ptr, nullptr) != 0)
+        return fail(err, err_len, ERT_E_ARGUMENT,
+                    "ert_attention_noalloc: the module was not compiled for heads_total=%u "
+                    "seq=%u head_dim=%u (no global %s); pass the shape of the attention IR "
+                    "it was compiled from",
+                    heads_total, seq, head_dim, shape_name);
 
     void *scratch = nullptr;
     int rc = scratch_address(&scratch, err, err_len);

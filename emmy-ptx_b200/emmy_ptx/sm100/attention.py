@@ -256,6 +256,12 @@ def pair_ok(comp, plan: AttnPlan) -> bool:
     return (PAIR and plan.dim in (64, 128) and plan.seq > BQ and g[0] % 2 == 0)
 
 
+def shape_global(heads_total: int, seq: int, head_dim: int) -> str:
+    """Name of the module global that records an attention module's compiled
+    shape ((batch*heads) x keys x head_dim)."""
+    return f"emmy_attn_shape_{heads_total}x{seq}x{head_dim}"
+
+
 # ----------------------------------------------------------------------------
 def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     """``gather`` > 0: the all-gather variant for a (batch x head) shard.
@@ -321,6 +327,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     b.module(".global .align 128 .b8 tmap_Khi[128];")
     b.module(".global .align 128 .b8 tmap_Klo[128];")
     b.module(".global .align 128 .b8 tmap_V[128];")
+    # the compiled shape, in a global's name: a launcher that brings its own
+    # tensor maps and scratch (libemmy_noalloc) looks this name up to refuse
+    # a shape the module was not compiled for, with no device read
+    b.module(f".visible .global .align 4 .u32 {shape_global(B * H, S, D)} = 1;")
     b.module(".extern .shared .align 1024 .b8 dsmem[];")
     if gather:
         b.module(f".global .align 8 .b8 emmy_gather_dst[{8 * gather}];")

@@ -45,12 +45,18 @@ extern "C" {
  *   err, err_len             receives a message on failure (may be NULL)
  *
  * Allocates nothing.  The first call on a device resolves the array's
- * address (once per device, with that device's context current); make that
- * call before any stream capture starts.  Returns ERT_E_TOO_LARGE, without
- * launching, when 2 * align256(heads_total*seq*head_dim*4) exceeds
- * ERT_NOALLOC_SCRATCH_BYTES; other codes as in emmy_rt.h.  Calls share the
- * scratch and rewrite the module's tensor-map globals: calls that overlap in
- * time race, so keep them on one stream. */
+ * address (once per device, with that device's context current; under lazy
+ * module loading this also loads the library's device image, and with it the
+ * array); make that call before any stream capture starts.  Returns
+ * ERT_E_TOO_LARGE, without launching, when
+ * 2 * align256(heads_total*seq*head_dim*4) exceeds ERT_NOALLOC_SCRATCH_BYTES,
+ * and ERT_E_ARGUMENT, without launching, when heads_total/seq/head_dim is not
+ * the shape `module` was compiled for (recorded in the module as the global
+ * emmy_attn_shape_<heads_total>x<seq>x<head_dim>); other codes as in
+ * emmy_rt.h.  Calls share the scratch and rewrite the module's tensor-map
+ * globals: calls that overlap in time race, so keep them on one stream, and
+ * do not also launch the same module through emmy_ptx.runtime.Kernel (it
+ * keeps the tensor maps it wrote and would run on the ones this call left). */
 int ert_attention_noalloc(uint64_t module, uint64_t attention_fn, uint64_t ksplit_fn,
                           const ert_geom *geom, void **args, uint64_t k, uint64_t v,
                           uint32_t heads_total, uint32_t seq, uint32_t head_dim,

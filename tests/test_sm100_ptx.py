@@ -118,6 +118,22 @@ def test_attention_module_carries_its_schedule(tmp_path):
     assert re.search(rf"setp\.eq\.u32 \S+, \S+, {side['grid'][0]};", ptx)
 
 
+def test_attention_module_records_its_compiled_shape(tmp_path):
+    """A launcher that brings its own scratch (ert_attention_noalloc) checks
+    the stated shape against the module's by looking up a global named for
+    the compiled (batch*heads) x keys x head_dim; the PTX assembles with it."""
+    from emmy_ptx import workloads
+    from emmy_ptx.sm100 import attention
+    p = workloads.attention(batch=2, heads=3, seq=200, head_dim=64, causal=True)
+    comp = Compiler(p.write(tmp_path), target="sm_100a", ptx_version="8.7")
+    ptx, _ = attention.emit(comp, attention.match(comp), pair=False)
+    name = attention.shape_global(6, 200, 64)
+    assert name == "emmy_attn_shape_6x200x64"
+    assert f".visible .global .align 4 .u32 {name} = 1;" in ptx
+    assert ptx.count("emmy_attn_shape_") == 1
+    _build.ptxas_check(ptx)
+
+
 def test_attention_epilogue_store_width_follows_the_isa_version(tmp_path):
     """32-byte stores (``st.global.v8.f32``) only from PTX ISA 8.8 on."""
     from emmy_ptx import workloads

@@ -105,17 +105,56 @@ def test_noalloc_matches_the_allocating_path(cuda):
     bh, seq, dim = 2 * 4, 320, 128
     stream = torch.cuda.current_stream().cuda_stream
     err = ctypes.create_string_buffer(512)
+    free_after = []
     for call in range(2):
         out.fill_(float("nan"))
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
         rc = lib.ert_attention_noalloc(k.module.handle.value, k.function, ksplit,
                                        ctypes.byref(geom), argv,
                                        dev["k"].data_ptr(), dev["v"].data_ptr(),
                                        bh, seq, dim, stream, err, len(err))
         assert rc == 0, err.value.decode()
         torch.cuda.synchronize()
+        free_after.append((free_before, torch.cuda.mem_get_info()[0]))
         assert k.status() == 0
         got = out.cpu().numpy()
         assert not np.isnan(got).any()
         ok, msg = check_close("attention", f"out (call {call + 1})", got, want, inputs)
         assert ok, msg
     assert not k.scratch, "the no-alloc path allocated runtime scratch"
+    # the device's free memory does not move across the second call (the
+    # first may load the library's device image, array included)
+    assert free_after[1][0] == free_after[1][1], free_after
+
+
+@pytest.mark.gpu
+def test_shape_other_than_the_compiled_one_is_refused(cuda):
+    """The pre-pass writes the element count compiled into the module, so a
+    smaller stated shape would pass the size check and then write past the
+    array.  The call refuses any shape but the compiled one, before it writes
+    a tensor map or launches (the output stays untouched)."""
+    import torch
+
+    p = workloads.attention(batch=1, heads=2, seq=256, head_dim=64)
+    ir = p.write(tempfile.mkdtemp(prefix="emmy_noalloc_shape_"))
+    k = rt.Kernel.from_ir(ir)
+    lib = _lib()
+    shape = p.tensor("out")["shape"]
+    inputs = {n: torch.from_numpy(v).to(cuda) for n, v in p.make_inputs().items()}
+    out = torch.full(shape, 3.0, device=cuda)
+    bufs = {**inputs, "out": out}
+    vals = [ctypes.c_uint64(bufs[a["name"]].data_ptr()) for a in k.args]
+    argv = (ctypes.c_void_p * len(vals))(*[ctypes.addressof(v) for v in vals])
+    geom = k.geometry("tuned")
+    ksplit = k.module.function(k.entry + "_ksplit")
+    err = ctypes.create_string_buffer(512)
+    for bh, seq, dim in [(2, 128, 64), (1, 256, 64), (2, 256, 32), (4, 256, 64)]:
+        rc = lib.ert_attention_noalloc(k.module.handle.value, k.function, ksplit,
+                                       ctypes.byref(geom), argv,
+                                       inputs["k"].data_ptr(), inputs["v"].data_ptr(),
+                                       bh, seq, dim, 0, err, len(err))
+        assert rc == -2, (bh, seq, dim, rc)
+        assert "not compiled for" in err.value.decode()
+    torch.cuda.synchronize()
+    assert bool((out == 3.0).all()), "a refused call launched the kernel"
