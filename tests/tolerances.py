@@ -10,6 +10,8 @@ f32 matmul (3xTF32 on tcgen05), and bf16/f16 matmul into f32:
 f32 attention:   |a - b| <= 1e-3 * (|b| + max_j |v_j| / sqrt(keys attended))
 """
 
+import math
+
 import numpy as np
 
 
@@ -79,3 +81,73 @@ def check_close(category, name, got, want, inputs=None, causal=True):
 def assert_close(category, name, got, want, inputs=None):
     ok, msg = check_close(category, name, got, want, inputs)
     assert ok, msg
+
+
+def check_close_device(category, name, got, want, inputs=None, causal=True, rows_per_chunk=None):
+    """The rules above on device tensors (torch, float64 arithmetic), in row
+    chunks so full-size outputs need no host copy and bounded scratch.
+    ``inputs`` holds device tensors.  Returns (ok, message)."""
+    import torch
+    if tuple(got.shape) != tuple(want.shape):
+        return False, f"{name}: shape {tuple(got.shape)} != {tuple(want.shape)}"
+    if not want.dtype.is_floating_point:
+        bad = got != want
+        nbad = int(bad.sum())
+        if nbad:
+            idx = tuple(int(i) for i in torch.nonzero(bad)[0])
+            return False, (f"{name}: {nbad} of {bad.numel()} integers differ; first at {idx}: "
+                           f"got {int(got[idx])}, want {int(want[idx])}")
+        return True, ""
+    # per-category tolerance parts that do not depend on the chunk
+    lead = want.shape[:-1]
+    if category == "matmul":
+        A, B = inputs["A"].double(), inputs["B"].double()
+        na = torch.linalg.vector_norm(A, dim=1)[:, None]
+        nb = torch.linalg.vector_norm(B, dim=0)[None, :]
+        cross = na * nb / math.sqrt(A.shape[1])
+    elif category == "attention":
+        seq = want.shape[-2]
+        vmax = inputs["v"].abs().amax(dim=(-1, -2)).double()          # [B, H]
+        keys = (torch.arange(1, seq + 1, device=want.device, dtype=torch.float64) if causal
+                else torch.full((seq,), float(seq), device=want.device, dtype=torch.float64))
+        cross = (vmax[..., None] / keys.sqrt())[..., None]            # [B, H, S, 1]
+    elif category == "colreduce_f64" and name != "colmax":
+        cross = 1e-12 * inputs["x"].abs().sum(0)
+    g2 = got.reshape(-1, want.shape[-1])
+    w2 = want.reshape(-1, want.shape[-1])
+    rows = g2.shape[0]
+    step = rows_per_chunk or max(1, (1 << 25) // want.shape[-1])
+    worst, nbad, first = 0.0, 0, None
+    for r0 in range(0, rows, step):
+        a = g2[r0:r0 + step].double()
+        b = w2[r0:r0 + step].double()
+        ab = b.abs()
+        if category in ("pointwise_f32", "pointwise"):
+            tol = 1e-5 * ab.clamp(min=1.0)
+        elif category == "rmsnorm":
+            tol = 1e-5 * ab.clamp(min=1e-3)
+        elif category == "softmax":
+            tol = 1e-5 * ab.clamp(min=1.0 / want.shape[-1])
+        elif category == "colreduce_f64":
+            tol = torch.zeros_like(ab) if name == "colmax" else cross.reshape(1, -1)
+        elif category == "matmul":
+            tol = 1e-3 * (ab + cross[r0:r0 + step])
+        elif category == "attention":
+            tol = 1e-3 * (ab + cross.reshape(-1, 1)[r0:r0 + step])
+        else:
+            tol = 1e-5 * ab.clamp(min=1.0)
+        err = (a - b).abs()
+        ok = (err <= tol) | (torch.isnan(a) & torch.isnan(b)) | (a == b)
+        n = int((~ok).sum())
+        if n and first is None:
+            i = torch.nonzero(~ok)[0]
+            first = (r0 + int(i[0]), int(i[1]), float(a[i[0], i[1]]), float(b[i[0], i[1]]))
+        nbad += n
+        e = err[~torch.isnan(err)]
+        if e.numel():
+            worst = max(worst, float(e.max()))
+    if nbad:
+        r, c, ga, wb = first
+        return False, (f"{name}: {nbad} of {want.numel()} values out of tolerance; first at "
+                       f"row {r} col {c}: got {ga!r}, want {wb!r}, max err {worst:.3g}")
+    return True, f"{name}: max err {worst:.3g}"
