@@ -7,27 +7,32 @@ Headline workload (the fused row kernels): one step is
 the RMSNorm kernel over x[8192, 4096] followed by the row-softmax kernel
 over logits[8192, 32768], both compiled from their Emmy IR packages by
 ``emmy_ptx.Compiler(target="sm_100a")`` and launched through the C ABI.
-``value`` = algorithmic HBM bytes of the step (every input read once, every
-output written once) / device time of the step, in GB/s, summed over ranks.
+``value`` = algorithmic HBM bytes of the whole config (every input read
+once, every output written once) / device time of the step, in GB/s.
 Inputs (2.4 GB per step) are larger than the 126 MB L2, so no flush is
 needed between steps.
 
-N > 1 (torchrun): weak scaling -- every rank runs its own full-size step on
-its own seeded rows; no collective sits in the data path.  The row-sharded
-variant of the north star (each rank 1/N of the rows, then an NCCL
-all-gather of the outputs) is timed separately and reported under
-``"sharded"`` (kernel-only and gather-inclusive).
+N > 1 (torchrun): strong scaling, the north star's sharded path -- every
+rank runs its 1/N of the rows of both kernels, then NCCL
+``all_gather_into_tensor`` puts both full outputs on every rank, inside
+the timed step (max over ranks).  The kernel-only time and the matmul /
+attention shards (NCCL gather vs the fused epilogue gather) are reported
+under ``"sharded"``.
 
-``--impl reference`` times the reference's own CPU semantics of the path --
-the oracle restatement (``oracle.simt``), since the reference compiler
-itself runs no kernels -- on the host cores, rank 0 only.
+``e2e`` is the same config through the host-buffer pipeline of the C ABI
+(pinned host rows -> device -> kernels -> pinned host, every step; each
+rank moves its own rows).
+
+The CPU baseline (``cpu_baseline`` at N=1, and ``--impl reference``) is the
+same computation with torch's CPU operators on every host core over the
+whole config (oracle/torch_cpu.py): the reference compiler itself runs no
+kernels, it writes PTX for an outside runner.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import sys
@@ -255,19 +260,25 @@ def link_gbs(device, nbytes=256 << 20, reps=3):
     return 2 * nbytes / best / 1e6
 
 
-def e2e_measure(names, workdir, steps, warmup, stream, seed_offset, chunks=8):
+def e2e_measure(names, workdir, steps, warmup, seed_offset, chunks=32, slots=3, rows_div=1):
     """The same step through the public host-buffer API: pinned host inputs
     -> device, the kernels, device -> pinned host outputs, every step.  Rows
-    are cut into ``chunks`` blocks on two streams so the copy-in, kernel and
-    copy-out of consecutive blocks overlap (emmy_ptx.pipeline)."""
-    import torch
-    from emmy_ptx import workloads
-    from emmy_ptx.pipeline import ChunkedHostRunner
-    from emmy_ptx.runtime import PinnedArray
+    are cut into ``chunks`` blocks; copy-in, kernels and copy-out run on three
+    streams of the C ABI, ordered per device slot by events
+    (emmy_ptx.pipeline), and the problems share the streams so one step's
+    copies never drain the link between problems."""
+    from emmy_ptx.pipeline import ChunkedHostRunner, PipelineStreams
+    from emmy_ptx.runtime import Event, PinnedArray
+    ps = PipelineStreams()
     runners = []
     total_bytes = 0
     for name in names:
-        r = ChunkedHostRunner(name, chunks=chunks, streams=2, workdir=workdir)
+        kw = {}
+        if rows_div > 1:          # this rank's 1/rows_div of the rows
+            from emmy_ptx import dist as edist
+            kw["rows"] = edist.FULL_DEFAULTS[name]["rows"] // rows_div
+        r = ChunkedHostRunner(name, chunks=chunks, slots=slots, workdir=workdir, streams=ps,
+                              **kw)
         p = r.full
         host = {}
         for n, arr in p.make_inputs(seed=p.seed + seed_offset).items():
@@ -281,96 +292,83 @@ def e2e_measure(names, workdir, steps, warmup, stream, seed_offset, chunks=8):
     for _ in range(warmup):
         for r, host, outs in runners:
             r.run(host, outs, sync=False)
-    torch.cuda.synchronize()
-    s, e = _events(2)
-    streams = runners[0][0].streams
-    s.record(stream)
-    for st in [x for r, _, _ in runners for x in r.streams]:
-        st.wait_event(s)
+    ps.synchronize()
+    start, end = Event(), Event()
+    marks = [Event() for _ in range(3)]
+    start.record(ps.h2d)
+    ps.after(start)
     h2d = d2h = 0
     for _ in range(steps):
         for r, host, outs in runners:
             r.run(host, outs, sync=False)
             h2d += r.last_bytes[0]
             d2h += r.last_bytes[1]
-    for st in [x for r, _, _ in runners for x in r.streams]:
-        ev = torch.cuda.Event()
-        ev.record(st)
-        stream.wait_event(ev)
-    e.record(stream)
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / steps
+    ps.join(ps.d2h, marks)
+    end.record(ps.d2h)
+    end.synchronize()
+    ms = start.elapsed_ms(end) / steps
     launches = sum(r.kernel.launches for r, _, _ in runners)
     for r, host, outs in runners:
         r.free()
         for pa in list(host.values()) + list(outs.values()):
             pa.free()
-    assert streams
+    for ev in [start, end] + marks:
+        ev.destroy()
+    ps.destroy()
     return {"ms_per_step": ms, "bytes": total_bytes, "h2d": h2d // steps, "d2h": d2h // steps,
-            "launches": launches, "chunks": chunks}
+            "launches": launches, "chunks": chunks, "slots": slots}
 
 
 # ----------------------------------------------------------------------------
-# CPU baseline: the oracle restatement on a bounded sample
+# CPU baseline: torch CPU operators over the whole configuration
 # ----------------------------------------------------------------------------
-SAMPLE_ROWS = {"rmsnorm": 128, "softmax": 16}
-
-
-def _oracle_chunk(args):
-    name, rows, seed = args
+def cpu_baseline(problems, steps, warmup, host_inputs=None):
+    """The headline step's computation with torch's CPU operators on every
+    host core (oracle/torch_cpu.py), over the whole configuration: RMSNorm
+    by formula on x[8192, 4096], then torch.softmax on [8192, 32768].
+    Median of ``steps`` timed steps after ``warmup``."""
+    import torch
     sys.path.insert(0, str(ROOT))
-    sys.path.insert(0, str(ROOT / "emmy-ptx_b200"))
-    from emmy_ptx import workloads
-    from oracle import simt
-    p = workloads.build(name, rows=rows)
-    inputs = p.make_inputs(seed=seed)
-    with tempfile.TemporaryDirectory() as td:
-        t0 = time.perf_counter()
-        simt.run_problem(p, inputs, td)
-        dt = time.perf_counter() - t0
-    return p.algorithmic_bytes(), dt
-
-
-def cpu_sample(processes=1, repeats=1, pool=None):
-    """Run the oracle over SAMPLE_ROWS rows of each headline kernel,
-    ``repeats`` chunks per worker; returns (bytes, seconds)."""
-    tasks = [(n, SAMPLE_ROWS[n], 100 + i) for i in range(processes * repeats) for n in HEADLINE]
-    t0 = time.perf_counter()
-    res = pool.map(_oracle_chunk, tasks) if pool is not None else [_oracle_chunk(t) for t in tasks]
-    wall = time.perf_counter() - t0
-    return sum(b for b, _ in res), wall
+    from oracle import torch_cpu
+    inputs = None
+    if host_inputs is not None:
+        inputs = [{k: torch.from_numpy(v) for k, v in h.items()} for h in host_inputs]
+    med, times, n = torch_cpu.time_problems(problems, steps, warmup, inputs=inputs)
+    nbytes = sum(p.algorithmic_bytes() for p in problems)
+    return {"value": round(nbytes / med / 1e9, 3), "unit": "GB/s", "cores": n,
+            "kind": "port", "engine": "torch-cpu",
+            "cpu": torch_cpu.cpu_model(),
+            "sample": f"the whole config-2 step (RMSNorm 8192x4096 + softmax 8192x32768, "
+                      f"{nbytes} algorithmic bytes) with torch {torch.__version__} CPU ops on "
+                      f"{n} threads; median of {steps} after {warmup} warm-up, "
+                      f"{statistics.median(times) * 1e3:.1f} ms per step"}
 
 
 # ----------------------------------------------------------------------------
 def run_reference(args):
+    """The reference arm.  The reference compiler runs no kernels of its own
+    (it writes PTX for an outside runner), so its CPU counterpart is the
+    computation its IR states, evaluated by torch's CPU operators on every
+    host core over the same configuration (oracle/torch_cpu.py).  Rank 0
+    only; other ranks exit without work."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    cores = len(os.sched_getaffinity(0))
-    import multiprocessing as mp
-    vals = []
-    total_b = total_s = 0.0
-    with mp.get_context("spawn").Pool(cores) as pool:
-        pool.map(_oracle_chunk, [("rmsnorm", 8, 1)] * cores)        # worker start-up
-        for i in range(args.warmup + args.steps):
-            b, s = cpu_sample(processes=cores, repeats=1, pool=pool)
-            if i >= args.warmup:
-                vals.append(b / s / 1e9)
-                total_b += b
-                total_s += s
-    value = statistics.median(vals)
-    sample = (f"per step: {cores} processes x (RMSNorm {SAMPLE_ROWS['rmsnorm']} rows x 4096 + "
-              f"softmax {SAMPLE_ROWS['softmax']} rows x 32768) through the oracle")
+    from emmy_ptx import workloads
+    problems = [workloads.build(n) for n in HEADLINE]
+    cb = cpu_baseline(problems, args.steps, args.warmup)
+    value = cb["value"]
+    step_bytes = sum(p.algorithmic_bytes() for p in problems)
     line = {
-        "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "impl": "reference",
+        "metric": METRIC, "value": value, "unit": "GB/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(total_s / max(1, args.steps) * 1000, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "ms_per_step": round(step_bytes / value / 1e6, 3),
+        "higher_is_better": True, "scaling": "strong" if args.gpus > 1 else "weak",
+        "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded torch.Generator inputs of the config's shapes)",
-        "config": {"workload": WORKLOAD, "sample": sample},
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores,
-                         "kind": "port", "sample": sample},
-        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+        "config": config_block(args.gpus),
+        "cpu_baseline": cb,
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -382,6 +380,10 @@ def categories_sweep(workdir, device, stream, pk):
     compiler's PTX on the same B200 (back-to-back launches)."""
     from emmy_ptx import workloads
     out = {}
+    tf32 = tf32_peak(device)
+    out["tf32_peak_tflops"] = {"value": round(tf32, 1),
+                               "how": "cuBLAS tf32 (torch.matmul, allow_tf32) 8192^3 f32 on this "
+                                      "GPU, best of 10 after 3 warm-up"}
     sweep = list(workloads.FULL_SIZE.items()) + [("16-/8-bit (beyond the BASELINE configs)",
                                                  ("matmul_bf16", "matmul_e4m3"))]
     for cfg, names in sweep:
@@ -406,13 +408,12 @@ def categories_sweep(workdir, device, stream, pk):
                 entry["frac_fp8_peak"] = round(mine.flops / ms / 1e9 / fp8, 3)
                 entry["fp8_peak"] = f"{fp8:.1f} TFLOP/s = 2 x measured bf16"
             elif compute:
-                tf32 = pk["bf16_tflops"] / 2
                 issued = mine.kernel.sidecar.get("tensor_flops_issued", mine.flops)
                 entry["tflops"] = round(mine.flops / ms / 1e9, 2)
                 entry["tflops_issued"] = round(issued / ms / 1e9, 2)
                 entry["frac_tf32_alg"] = round(mine.flops / ms / 1e9 / tf32, 3)
                 entry["frac_tf32_issued"] = round(issued / ms / 1e9 / tf32, 3)
-                entry["tf32_peak"] = f"{tf32:.1f} TFLOP/s = measured bf16 / 2"
+                entry["tf32_peak"] = f"{tf32:.1f} TFLOP/s (measured cuBLAS tf32, this GPU)"
             else:
                 entry["gbs"] = round(mine.bytes / ms / 1e6, 1)
                 entry["frac_hbm"] = round(mine.bytes / ms / 1e6 / pk["hbm_gbs"], 3)
@@ -434,6 +435,120 @@ def categories_sweep(workdir, device, stream, pk):
     return out
 
 
+def config_block(world):
+    c = {"workload": WORKLOAD, "rows_total": 8192, "rows_per_rank": 8192 // world,
+         "l2": "inputs larger than L2 (2.4 GB per step at N=1; at N>1 each rank's shard "
+               "plus the 1.2 GB of gathered outputs)"}
+    if world > 1:
+        c["exchange"] = ("each rank runs its 1/N of the rows of both kernels, then "
+                         "all_gather_into_tensor (NCCL) of both outputs into the full "
+                         "outputs on every rank, inside the timed step")
+        c["parallelism"] = f"rows/{world}"
+    return c
+
+
+class HeadlineStep:
+    """The headline step on this rank.  N=1: the whole config.  N>1 (strong
+    scaling): this rank's 1/N of the rows of every problem (each rank's rows
+    seeded on their own), then an NCCL all-gather of every output into the
+    full output, on the same stream."""
+
+    def __init__(self, workdir, device, stream, rank, world):
+        import torch
+        from emmy_ptx import workloads
+        self.world, self.stream = world, stream
+        rows = {n: workloads.build(n).tensor(workloads.build(n).inputs[0])["shape"][0]
+                for n in HEADLINE}
+        self.bounds = [Bound(n, workdir, device, stream, seed_offset=rank,
+                             rows=rows[n] // world if world > 1 else None) for n in HEADLINE]
+        self.full_bytes = sum(workloads.build(n).algorithmic_bytes() for n in HEADLINE)
+        self.outs, self.gathered = [], []
+        if world > 1:
+            for b in self.bounds:
+                for o in b.problem.outputs:
+                    t = b.dev[o]
+                    self.outs.append(t.reshape(-1))
+                    self.gathered.append(torch.empty(world * t.numel(), dtype=t.dtype,
+                                                     device=device))
+
+    def launch_marked(self, marks=None):
+        """Queue one step; record ``marks[i]`` after kernel i and the last
+        mark after the gathers."""
+        import torch.distributed as dist
+        for i, b in enumerate(self.bounds):
+            b.launch()
+            if marks is not None:
+                marks[i].record(self.stream)
+        for g, t in zip(self.gathered, self.outs):
+            dist.all_gather_into_tensor(g, t)
+        if marks is not None:
+            marks[len(self.bounds)].record(self.stream)
+
+
+def time_headline(hs, steps, warmup, barrier):
+    """W warm-up steps, then K timed steps bracketed by barrier + sync; CUDA
+    events on the launching stream.  Returns (step ms, per-kernel ms,
+    gather ms)."""
+    import torch
+    stream = hs.stream
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            hs.launch_marked()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    nb = len(hs.bounds)
+    start = _events(1)[0]
+    marks = [_events(nb + 1) for _ in range(steps)]
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for k in range(steps):
+            hs.launch_marked(marks[k])
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    total = start.elapsed_time(marks[-1][-1])
+    per = [0.0] * nb
+    gather = 0.0
+    prev = start
+    for k in range(steps):
+        for j in range(nb):
+            per[j] += prev.elapsed_time(marks[k][j])
+            prev = marks[k][j]
+        gather += prev.elapsed_time(marks[k][nb])
+        prev = marks[k][nb]
+    return total / steps, [x / steps for x in per], gather / steps
+
+
+def tf32_peak(device, n=8192, reps=10):
+    """cuBLAS tf32 throughput (torch.matmul, allow_tf32) at n^3 on this GPU,
+    best of ``reps`` after warm-up: the denominator for the tf32 tensor-core
+    kernels.  2 n^3 flop per product."""
+    import torch
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    try:
+        g = torch.Generator(device=device).manual_seed(0)
+        a = torch.rand(n, n, device=device, generator=g)
+        b = torch.rand(n, n, device=device, generator=g)
+        for _ in range(3):
+            torch.matmul(a, b)
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(reps):
+            s, e = _events(2)
+            s.record()
+            torch.matmul(a, b)
+            e.record()
+            torch.cuda.synchronize()
+            t = s.elapsed_time(e)
+            best = t if best is None else min(best, t)
+        del a, b
+        return 2 * n ** 3 / best / 1e9
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -452,23 +567,26 @@ def run_b200(args):
         if world > 1:
             dist.barrier()
 
+    def max_over_ranks(x):
+        t = torch.tensor([float(x)], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     pk = peaks()
     stream = torch.cuda.Stream(device)
     workdir = tempfile.mkdtemp(prefix="emmy_bench_")
-    bounds = [Bound(n, workdir, device, stream, seed_offset=rank) for n in HEADLINE]
+    hs = HeadlineStep(workdir, device, stream, rank, world)
     clocks = Clocks(local)
     clocks.start()
-    step_ms, per_kernel = time_steps(bounds, args.steps, args.warmup, stream, barrier)
+    step_ms, per_kernel, gather_ms = time_headline(hs, args.steps, args.warmup, barrier)
     clk = clocks.stop()
+    bounds = hs.bounds
     launches = args.steps * len(bounds)
-    t = torch.tensor([step_ms], device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms = float(t.item())
-    step_bytes = sum(b.bytes for b in bounds)
-    value = world * step_bytes / step_ms / 1e6
+    step_ms = max_over_ranks(step_ms)
+    value = hs.full_bytes / step_ms / 1e6
 
-    # dominant kernel (largest share of the step): roofline
+    # dominant kernel (largest share of the kernels' time): roofline
     j = max(range(len(bounds)), key=lambda i: per_kernel[i])
     dom = bounds[j]
     achieved = dom.bytes / per_kernel[j] / 1e6
@@ -478,33 +596,43 @@ def run_b200(args):
                 "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)"
                 if pk["source"] == "measured" else "fallback 6650 GB/s",
                 "algorithmic_bytes_per_launch": dom.bytes,
-                "ms_per_launch": round(per_kernel[j], 4),
-                "traffic": _traffic(dom.kernel.entry)}
+                "ms_per_launch": round(per_kernel[j], 4)}
+    roofline.update(_traffic(dom.kernel.entry, dom.bytes))
     kernels = {b.kernel.entry: {"ms": round(per_kernel[i], 4),
                                 "gbs": round(b.bytes / per_kernel[i] / 1e6, 1),
                                 "frac": round(b.bytes / per_kernel[i] / 1e6 / pk["hbm_gbs"], 4)}
                for i, b in enumerate(bounds)}
-    del bounds
+    hosts = [b.host for b in bounds] if world == 1 else None
+    problems = [b.problem for b in bounds]
+    del bounds, hs
     torch.cuda.empty_cache()
 
-    e2e = e2e_measure(HEADLINE, workdir, max(2, args.steps // 4), 1, stream, rank)
-    et = torch.tensor([e2e["ms_per_step"]], device=device)
+    # end to end through the host-buffer API: each rank moves its own rows
+    chunks = max(4, 32 // world)
+    barrier()
+    e2e = e2e_measure(HEADLINE, workdir, max(3, args.steps // 4), 2, rank,
+                      chunks=chunks, rows_div=world)
+    et = max_over_ranks(e2e["ms_per_step"])
+    e2e_value = world * e2e["bytes"] / et / 1e6
+    # every rank's link, both ways at once, all ranks copying together
+    barrier()
+    mine = link_gbs(device)
+    links = [mine]
     if world > 1:
-        dist.all_reduce(et, op=dist.ReduceOp.MAX)
-    e2e_value = world * e2e["bytes"] / float(et.item()) / 1e6
-    # this rank's link, both ways at once; the slowest rank's for the job
-    lk = torch.tensor([link_gbs(device)], device=device)
-    if world > 1:
-        dist.all_reduce(lk, op=dist.ReduceOp.MIN)
-    link = float(lk.item())
-    pcie_gbs = (e2e["h2d"] + e2e["d2h"]) / float(et.item()) / 1e6     # per rank
-    launches_total = launches
+        allv = [None] * world
+        dist.all_gather_object(allv, mine)
+        links = allv
+    link_total = sum(links)
+    pcie_total = world * (e2e["h2d"] + e2e["d2h"]) / et / 1e6
 
     sharded = None
     if world > 1:
         from emmy_ptx import dist as edist
-        sharded = edist.bench_sharded(HEADLINE, workdir, device, stream, rank, world,
-                                      steps=max(3, args.steps // 2), warmup=2)
+        sharded = {"config2_kernel_only": {
+            "ms": round(max_over_ranks(sum(per_kernel)), 4),
+            "gbs": round(sum(p.algorithmic_bytes() for p in problems) * world
+                         / max_over_ranks(sum(per_kernel)) / 1e6, 1),
+            "gather_ms": round(max_over_ranks(gather_ms), 4)}}
         # matmul 8192^3 in row blocks and causal attention 8x32x4096x128 in
         # (batch x head) pairs: NCCL all-gather vs the fused epilogue gather
         for name in ("matmul", "attention"):
@@ -512,7 +640,7 @@ def run_b200(args):
             # on every rank at the same step and is reported, not fatal
             try:
                 sharded[name] = edist.bench_fused_gather(name, workdir, device, stream, rank,
-                                                         world, steps=5, warmup=2)
+                                                         world, steps=5, warmup=3)
             except Exception as exc:  # noqa: BLE001
                 sharded[name] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
             torch.cuda.empty_cache()
@@ -520,36 +648,33 @@ def run_b200(args):
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded torch.Generator inputs of the config's shapes)",
-        "config": {"workload": WORKLOAD, "rows_per_rank": 8192,
-                   "l2": "inputs larger than L2 (2.4 GB per step)",
-                   "launch": "sm_100a PTX via libemmy_rt C ABI (cuLaunchKernelEx)"},
+        "config": config_block(world),
+        "launch": "sm_100a PTX via libemmy_rt C ABI (cuLaunchKernelEx)",
         "kernels": kernels,
         "roofline": roofline,
         "clocks": clk,
-        "gpu_launches": launches_total,
+        "gpu_launches": launches,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                "ms_per_step": round(e2e["ms_per_step"], 3),
-                "link_both_ways_gbs": round(link, 1),
-                "frac_of_link": round(pcie_gbs / link, 3),
-                "path": f"emmy_ptx.pipeline.ChunkedHostRunner: pinned host -> cuMemcpyHtoDAsync "
-                        f"-> launch -> cuMemcpyDtoHAsync, {e2e['chunks']} row blocks on 2 streams"},
+                "h2d_bytes_per_step": e2e["h2d"] * world, "d2h_bytes_per_step": e2e["d2h"] * world,
+                "ms_per_step": round(et, 3),
+                "link_both_ways_gbs": round(link_total, 1),
+                "link_per_rank_gbs": [round(x, 1) for x in links],
+                "frac_of_link": round(pcie_total / link_total, 3),
+                "path": f"emmy_ptx.pipeline.ChunkedHostRunner: pinned host -> ert_memcpy_htod "
+                        f"-> launch -> ert_memcpy_dtoh, {e2e['chunks']} row blocks per rank "
+                        f"over {e2e['slots']} device slots on three C-ABI streams"},
     }
+    if world > 1:
+        line["gather_ms_per_step"] = round(max_over_ranks(gather_ms), 4)
     if sharded is not None:
         line["sharded"] = sharded
     if rank == 0 and world == 1:
         if not args.no_categories:
             line["categories"] = categories_sweep(workdir, device, stream, pk)
-        b, s = cpu_sample(processes=1, repeats=1)
-        reps = max(1, int(math.ceil(10.0 / max(s, 1e-3))))
-        b, s = cpu_sample(processes=1, repeats=min(reps, 40))
-        line["cpu_baseline"] = {
-            "value": round(b / s / 1e9, 5), "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"oracle.simt (numpy IR interpreter), {min(reps, 40)} x "
-                      f"(RMSNorm {SAMPLE_ROWS['rmsnorm']} rows + softmax "
-                      f"{SAMPLE_ROWS['softmax']} rows), {s:.1f} s"}
+        line["cpu_baseline"] = cpu_baseline(problems, 5, 1, host_inputs=hosts)
     if rank == 0:
         print(json.dumps(line))
     if world > 1:
@@ -558,13 +683,21 @@ def run_b200(args):
     return 0
 
 
-def _traffic(entry):
-    """DRAM bytes per launch of ``entry`` from the committed ncu summary."""
+def _traffic(entry, algorithmic_bytes):
+    """DRAM bytes per launch of ``entry`` from the committed full-size ncu
+    capture (profiles/traffic.json: ``dram__bytes_read.sum +
+    dram__bytes_write.sum`` of a steady-state launch, with the previous
+    launch's dirty L2 lines written back inside it), scaled to this launch's
+    algorithmic bytes when the launch is a row shard (traffic of a row kernel
+    grows in proportion to its rows)."""
     f = ROOT / "profiles" / "traffic.json"
     try:
-        return json.loads(f.read_text()).get(entry)
+        rec = json.loads(f.read_text())[entry]
     except Exception:  # noqa: BLE001
-        return None
+        return {"traffic": None}
+    t = rec["dram_bytes_per_launch"] * algorithmic_bytes / rec["algorithmic_bytes"]
+    return {"traffic": int(t), "traffic_over_algorithmic": round(t / algorithmic_bytes, 4),
+            "traffic_source": rec["summary"]}
 
 
 def run_kernel_only(args):

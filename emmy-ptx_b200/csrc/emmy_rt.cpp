@@ -53,6 +53,9 @@ struct Driver {
     ERT_FN(cuMemcpyDtoHAsync)
     ERT_FN(cuMemsetD8Async)
     ERT_FN(cuStreamSynchronize)
+    ERT_FN(cuStreamCreate)
+    ERT_FN(cuStreamDestroy)
+    ERT_FN(cuStreamWaitEvent)
     ERT_FN(cuMemAlloc)
     ERT_FN(cuMemFree)
     ERT_FN(cuMemHostAlloc)
@@ -61,6 +64,7 @@ struct Driver {
     ERT_FN(cuEventRecord)
     ERT_FN(cuEventElapsedTime)
     ERT_FN(cuEventDestroy)
+    ERT_FN(cuEventSynchronize)
     ERT_FN(cuIpcGetMemHandle)
     ERT_FN(cuIpcOpenMemHandle)
     ERT_FN(cuIpcCloseMemHandle)
@@ -97,6 +101,9 @@ struct Driver {
         ERT_LOAD(cuMemcpyDtoHAsync)
         ERT_LOAD(cuMemsetD8Async)
         ERT_LOAD(cuStreamSynchronize)
+        ERT_LOAD(cuStreamCreate)
+        ERT_LOAD(cuStreamDestroy)
+        ERT_LOAD(cuStreamWaitEvent)
         ERT_LOAD(cuMemAlloc)
         ERT_LOAD(cuMemFree)
         ERT_LOAD(cuMemHostAlloc)
@@ -105,6 +112,7 @@ struct Driver {
         ERT_LOAD(cuEventRecord)
         ERT_LOAD(cuEventElapsedTime)
         ERT_LOAD(cuEventDestroy)
+        ERT_LOAD(cuEventSynchronize)
         ERT_LOAD(cuIpcGetMemHandle)
         ERT_LOAD(cuIpcOpenMemHandle)
         ERT_LOAD(cuIpcCloseMemHandle)
@@ -383,6 +391,34 @@ int ert_stream_sync(uint64_t stream) {
                  "cuStreamSynchronize");
 }
 
+int ert_stream_create(uint64_t *stream) {
+    ERT_NEED_DRIVER();
+    if (!stream) return fail(ERT_E_ARGUMENT, "stream is null");
+    int rc;
+    if ((rc = need_ctx())) return rc;
+    CUstream s = nullptr;
+    // non-blocking: no implicit ordering against the legacy default stream,
+    // so copies on one such stream overlap work on the others
+    if ((rc = check(drv().cuStreamCreate(&s, CU_STREAM_NON_BLOCKING), "cuStreamCreate")))
+        return rc;
+    *stream = reinterpret_cast<uint64_t>(s);
+    return 0;
+}
+
+int ert_stream_destroy(uint64_t stream) {
+    ERT_NEED_DRIVER();
+    if (!stream) return fail(ERT_E_ARGUMENT, "stream is null (the default stream is not owned)");
+    return check(drv().cuStreamDestroy(reinterpret_cast<CUstream>(stream)), "cuStreamDestroy");
+}
+
+int ert_stream_wait_event(uint64_t stream, uint64_t event) {
+    ERT_NEED_DRIVER();
+    if (!event) return fail(ERT_E_ARGUMENT, "event is null");
+    return check(drv().cuStreamWaitEvent(reinterpret_cast<CUstream>(stream),
+                                         reinterpret_cast<CUevent>(event), 0),
+                 "cuStreamWaitEvent");
+}
+
 int ert_mem_alloc(uint64_t *dptr, size_t bytes) {
     ERT_NEED_DRIVER();
     if (!dptr) return fail(ERT_E_ARGUMENT, "dptr is null");
@@ -477,6 +513,13 @@ int ert_event_elapsed(uint64_t start, uint64_t end, float *ms) {
     return check(drv().cuEventElapsedTime(ms, reinterpret_cast<CUevent>(start),
                                           reinterpret_cast<CUevent>(end)),
                  "cuEventElapsedTime");
+}
+
+int ert_event_sync(uint64_t event) {
+    ERT_NEED_DRIVER();
+    if (!event) return fail(ERT_E_ARGUMENT, "event is null");
+    return check(drv().cuEventSynchronize(reinterpret_cast<CUevent>(event)),
+                 "cuEventSynchronize");
 }
 
 int ert_event_destroy(uint64_t event) {

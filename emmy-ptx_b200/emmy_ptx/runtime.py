@@ -74,6 +74,9 @@ _SIGS = {
     "ert_memset_d8": ([ctypes.c_uint64, ctypes.c_ubyte, ctypes.c_size_t, ctypes.c_uint64],
                       ctypes.c_int),
     "ert_stream_sync": ([ctypes.c_uint64], ctypes.c_int),
+    "ert_stream_create": ([ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "ert_stream_destroy": ([ctypes.c_uint64], ctypes.c_int),
+    "ert_stream_wait_event": ([ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
     "ert_mem_alloc": ([ctypes.POINTER(ctypes.c_uint64), ctypes.c_size_t], ctypes.c_int),
     "ert_mem_free": ([ctypes.c_uint64], ctypes.c_int),
     "ert_ipc_get_handle": ([ctypes.c_uint64, ctypes.c_void_p], ctypes.c_int),
@@ -85,6 +88,7 @@ _SIGS = {
     "ert_event_record": ([ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int),
     "ert_event_elapsed": ([ctypes.c_uint64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_float)],
                           ctypes.c_int),
+    "ert_event_sync": ([ctypes.c_uint64], ctypes.c_int),
     "ert_event_destroy": ([ctypes.c_uint64], ctypes.c_int),
     "ert_status": ([ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint64],
                    ctypes.c_int),
@@ -179,6 +183,60 @@ def _ptr(x) -> int:
     if dp is None:
         raise TypeError(f"not a device buffer: {type(x).__name__}")
     return int(dp())
+
+
+class Stream:
+    """A non-blocking CUDA stream owned through the C ABI
+    (``ert_stream_create``), usable wherever a stream is accepted."""
+
+    def __init__(self):
+        h = ctypes.c_uint64(0)
+        check(lib().ert_stream_create(ctypes.byref(h)), "ert_stream_create")
+        self.handle = h.value
+
+    @property
+    def cuda_stream(self) -> int:
+        return self.handle
+
+    def wait(self, event: "Event"):
+        """Later work on this stream waits for ``event``'s last record."""
+        check(lib().ert_stream_wait_event(self.handle, event.handle), "ert_stream_wait_event")
+
+    def synchronize(self):
+        check(lib().ert_stream_sync(self.handle), "ert_stream_sync")
+
+    def destroy(self):
+        if self.handle:
+            check(lib().ert_stream_destroy(self.handle), "ert_stream_destroy")
+            self.handle = 0
+
+
+class Event:
+    """A CUDA event through the C ABI (timing and stream ordering)."""
+
+    def __init__(self):
+        h = ctypes.c_uint64(0)
+        check(lib().ert_event_create(ctypes.byref(h)), "ert_event_create")
+        self.handle = h.value
+        self.recorded = False
+
+    def record(self, stream=None):
+        check(lib().ert_event_record(self.handle, _stream_handle(stream)), "ert_event_record")
+        self.recorded = True
+
+    def synchronize(self):
+        check(lib().ert_event_sync(self.handle), "ert_event_sync")
+
+    def elapsed_ms(self, end: "Event") -> float:
+        ms = ctypes.c_float(0)
+        check(lib().ert_event_elapsed(self.handle, end.handle, ctypes.byref(ms)),
+              "ert_event_elapsed")
+        return ms.value
+
+    def destroy(self):
+        if self.handle:
+            check(lib().ert_event_destroy(self.handle), "ert_event_destroy")
+            self.handle = 0
 
 
 class Module:
@@ -546,6 +604,6 @@ def load_sidecar(path) -> dict:
     return json.loads(Path(path).read_text())
 
 
-__all__ = ["Kernel", "Module", "HostRunner", "PinnedArray", "DeviceBuffer", "LaunchSequence", "init",
+__all__ = ["Kernel", "Module", "Stream", "Event", "HostRunner", "PinnedArray", "DeviceBuffer", "LaunchSequence", "init",
            "ipc_handle", "ipc_open", "ipc_close",
            "device_count", "EmmyRuntimeError", "LIB_PATH", "EXPORTED"]

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define ERT_ABI_VERSION 1
+#define ERT_ABI_VERSION 2
 
 #define ERT_E_NO_DRIVER   (-1)  /* libcuda.so.1 missing or a symbol absent */
 #define ERT_E_ARGUMENT    (-2)  /* invalid argument (null pointer, bad size) */
@@ -91,6 +91,16 @@ int ert_memcpy_dtoh(void *dst, uint64_t src, size_t bytes, uint64_t stream);
 int ert_memset_d8(uint64_t dst, unsigned char value, size_t bytes, uint64_t stream);
 int ert_stream_sync(uint64_t stream);
 
+/* Streams of the caller's own (non-blocking: not ordered against the legacy
+ * default stream), for callers without another CUDA runtime.  The
+ * host-buffer pipeline uses one for host->device copies, one for launches
+ * and one for device->host copies, ordered by events. */
+int ert_stream_create(uint64_t *stream);
+int ert_stream_destroy(uint64_t stream);
+/* Work submitted to `stream` after this call waits for `event`'s last
+ * record (cuStreamWaitEvent). */
+int ert_stream_wait_event(uint64_t stream, uint64_t event);
+
 /* Device memory for callers that do not bring their own allocator. */
 int ert_mem_alloc(uint64_t *dptr, size_t bytes);
 int ert_mem_free(uint64_t dptr);
@@ -107,10 +117,12 @@ int ert_ipc_get_handle(uint64_t dptr, void *handle);
 int ert_ipc_open(const void *handle, uint64_t *dptr);
 int ert_ipc_close(uint64_t dptr);
 
-/* CUDA events for timing on a stream. */
+/* CUDA events, for timing on a stream and for ordering streams. */
 int ert_event_create(uint64_t *event);
 int ert_event_record(uint64_t event, uint64_t stream);
 int ert_event_elapsed(uint64_t start, uint64_t end, float *ms);
+/* Block the calling thread until `event`'s last record has completed. */
+int ert_event_sync(uint64_t event);
 int ert_event_destroy(uint64_t event);
 
 /* Read and clear the module's `emmy_status` word (0 = ok).  Kernels with

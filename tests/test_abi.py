@@ -32,7 +32,16 @@ def test_python_binding_covers_the_header():
 
 
 def test_abi_version():
-    assert rt.lib().ert_abi_version() == 1
+    assert rt.lib().ert_abi_version() == 2
+
+
+def test_streams_and_events_are_on_the_abi():
+    """A C caller can run the host-buffer pipeline (copies and launches on
+    streams of its own, ordered by events) without another CUDA runtime."""
+    names = declared()
+    for n in ("ert_stream_create", "ert_stream_destroy", "ert_stream_wait_event",
+              "ert_event_create", "ert_event_record", "ert_event_sync", "ert_event_destroy"):
+        assert n in names, n
 
 
 def test_no_driver_is_an_error_not_a_crash():

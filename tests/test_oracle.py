@@ -156,3 +156,28 @@ def test_out_of_bounds_access_is_reported():
         with pytest.raises(OracleError, match="out-of-bounds"):
             simt.run_problem(p, p.make_inputs(), td)
     assert BinaryExpr and Literal
+
+
+TORCH_CPU_TAGS = [t for t, (name, _) in cases.PARITY.items()
+                  if name in ("pointwise_f32", "pointwise_i32", "rmsnorm", "softmax",
+                              "colreduce_f64", "rowsum_i32", "matmul", "attention")]
+
+
+@pytest.mark.parametrize("tag", TORCH_CPU_TAGS)
+def test_torch_cpu_baseline_matches_reference_gpu_vectors(tag):
+    """The timed CPU baseline (torch CPU operators, oracle/torch_cpu.py)
+    computes what the reference's PTX computed on the B200: integers bit for
+    bit (truncating int32 division, as the reference lowers it), floats within
+    the parity tolerances."""
+    import torch
+    from oracle import torch_cpu
+    p = cases.problem(tag)
+    if not p.params.get("causal", True):
+        pytest.skip("the CPU baseline times the causal configuration")
+    gold = np.load(VECTORS / f"{tag}.npz")
+    inputs = p.make_inputs()
+    got = torch_cpu.run(p.category, {k: torch.from_numpy(v) for k, v in inputs.items()},
+                        p.params)
+    for o in p.outputs:
+        ok, msg = check_close(p.category, o, got[o].numpy(), gold[o], inputs)
+        assert ok, msg
