@@ -52,15 +52,11 @@ def main(argv=None) -> int:
         return 0
 
     try:
-        if args.output:
-            comp = Compiler(args.ir_path, target=args.target, ptx_version=args.ptx_version)
-            ptx = comp.compile()
-            sidecar = comp.sidecar()
-        else:
-            from .compiler import compile_file
-            ptx = compile_file(args.ir_path, target=args.target,
-                               ptx_version=args.ptx_version, cache_dir=args.cache_dir)
-            sidecar = None
+        # every path goes through the cache, as the reference's does
+        # (cli.py:50-66): ``-o`` only changes where the PTX is written
+        from .compiler import compile_cached
+        ptx, sidecar = compile_cached(args.ir_path, target=args.target,
+                                      ptx_version=args.ptx_version, cache_dir=args.cache_dir)
     except (SystemExit, ValueError, Exception) as exc:  # noqa: BLE001
         print(str(exc), file=sys.stderr)
         return 1

@@ -292,18 +292,33 @@ def compile_file(path, *, target: str = "sm_89", ptx_version: str = "8.0",
                  cache_dir=None) -> str:
     """Compile ``path``; with ``cache_dir`` the PTX (and its launch sidecar,
     ``<key>.json``) is cached by IR hash."""
+    return compile_cached(path, target=target, ptx_version=ptx_version, cache_dir=cache_dir)[0]
+
+
+def compile_cached(path, *, target: str = "sm_89", ptx_version: str = "8.0",
+                   cache_dir=None):
+    """``compile_file`` that also returns the launch sidecar: ``(ptx,
+    sidecar)``.  On a cache hit both come from the cache (``<key>.ptx`` and
+    ``<key>.json``); the sidecar is None if the cache holds none."""
     if cache_dir is not None:
         os.makedirs(cache_dir, exist_ok=True)
         key = _cache_key(path, target, ptx_version)
         cache_path = os.path.join(cache_dir, key + ".ptx")
+        side_path = os.path.join(cache_dir, key + ".json")
         if os.path.exists(cache_path):
             with open(cache_path) as f:
-                return f.read()
+                ptx = f.read()
+            sidecar = None
+            if os.path.exists(side_path):
+                with open(side_path) as f:
+                    sidecar = json.load(f)
+            return ptx, sidecar
     comp = Compiler(path, target=target, ptx_version=ptx_version)
     result = comp.compile()
+    sidecar = comp.sidecar()
     if cache_dir is not None:
         with open(cache_path, "w") as f:
             f.write(result)
-        with open(os.path.join(cache_dir, key + ".json"), "w") as f:
-            json.dump(comp.sidecar(), f, indent=1)
-    return result
+        with open(side_path, "w") as f:
+            json.dump(sidecar, f, indent=1)
+    return result, sidecar

@@ -216,13 +216,17 @@ class Ops:
         return self._f("selp.f32 {0}, 0f3F800000, {1}, " + p_00 + ";", out)
 
     # -- integer division ------------------------------------------------------
-    def _idiv(self, a, bb):
-        key = (a, bb)
+    def _idiv(self, a, bb, floor=False):
+        """Quotient of a / bb: truncating (``div.s32``, the reference's
+        lowering), or floored for ``floor_divide``/``remainder`` under
+        ``int_semantics="torch"``."""
+        floor = floor and self.int_semantics == "torch"
+        key = (a, bb, floor)
         if key in self._quot:
             return self._quot[key]
         q = self.b.reg("r")
         self.b.ins(f"div.s32 {q}, {a}, {bb};")
-        if self.int_semantics == "torch":
+        if floor:
             # floor: subtract one when the remainder is nonzero and has the
             # opposite sign of the divisor
             prod, r, x = self.b.regs("r", 3)
@@ -241,7 +245,7 @@ class Ops:
         return q
 
     def _irem(self, a, bb):
-        q = self._idiv(a, bb)
+        q = self._idiv(a, bb, floor=True)
         prod = self.b.reg("r")
         self.b.ins(f"mul.lo.s32 {prod}, {q}, {bb};")
         r = self.b.reg("r")
@@ -373,7 +377,7 @@ class Ops:
             return out, dt
         regs = [self.coerce(a, "s32") for a in args]
         if name in ("divide", "true_divide", "floor_divide"):
-            return self._idiv(regs[0], regs[1]), "s32"
+            return self._idiv(regs[0], regs[1], floor=name == "floor_divide"), "s32"
         if name in ("remainder", "mod"):
             return self._irem(regs[0], regs[1]), "s32"
         ins = self._IBIN.get(name)

@@ -246,6 +246,25 @@ def div_s32(a, b):
     return np.where(b == 0, -1, q).astype(np.int64).astype(np.int32)
 
 
+def floor_div_s32(a, b):
+    """``floor_divide`` on int32 under the backend's ``int_semantics="torch"``:
+    the truncating quotient, less one when the remainder is nonzero and its
+    sign differs from the divisor's -- torch's floor division for b != 0.
+    Restated from the fix-up the backend emits after ``div.s32`` (so b == 0
+    gives what that sequence gives, with div.s32's -1 quotient)."""
+    q = div_s32(a, b).astype(np.int64)
+    r = _wrap32(np.asarray(a, np.int64) - _wrap32(q * np.asarray(b, np.int64)))
+    fix = (r != 0) & ((r.astype(np.int64) ^ np.asarray(b, np.int64)) < 0)
+    return _wrap32(q - fix.astype(np.int64))
+
+
+def floor_rem_s32(a, b):
+    """``remainder`` under ``int_semantics="torch"``: a - floor_div(a, b) * b,
+    which has the divisor's sign (torch.remainder) for b != 0."""
+    q = floor_div_s32(a, b).astype(np.int64)
+    return _wrap32(np.asarray(a, np.int64) - _wrap32(q * np.asarray(b, np.int64)))
+
+
 def rem_s32(a, b):
     """rem.s32: sign of the dividend (compiler.py:798, 1384)."""
     a64 = np.asarray(a, np.int64)
@@ -343,11 +362,14 @@ _CMP = {"greater": np.greater, "greater_equal": np.greater_equal,
         "not_equal": np.not_equal}
 
 
-def op_on_values(name, args, arg_dts, dtype="f32"):
+def op_on_values(name, args, arg_dts, dtype="f32", int_semantics="reference"):
     """The value of elementwise op ``name`` (compiler.py:1047-1404).
 
     ``args`` are lane arrays with dtypes ``arg_dts``; ``dtype`` is the
-    statement's dtype.  Returns ``(value, dtype)``.
+    statement's dtype.  Returns ``(value, dtype)``.  ``int_semantics``
+    "torch" gives int32 ``floor_divide``/``remainder`` torch's floored
+    meaning, as the backend's option of that name does; the default is the
+    reference's truncating ``div.s32``/``rem.s32``.
     """
     name = getattr(name, "name", str(name))
     dt = dtype_name(dtype) or "f32"
@@ -485,6 +507,9 @@ def op_on_values(name, args, arg_dts, dtype="f32"):
     if op is None:
         raise OracleError(f"unsupported integer op {name!r}")
     args = [coerce(a, d, "s32") for a, d in zip(args, arg_dts)]
+    if int_semantics == "torch" and name in ("floor_divide", "remainder", "mod"):
+        f = floor_div_s32 if name == "floor_divide" else floor_rem_s32
+        return f(args[0], args[1]), "s32"
     return _int_arith(op, args[0], args[1]), "s32"
 
 

@@ -53,8 +53,9 @@ class Interpreter:
     """Runs one KernelOp over a 1-D launch of ``grid x block`` threads."""
 
     def __init__(self, kernel: I.KernelOp, tensors: dict, args: dict,
-                 grid: int, block: int):
+                 grid: int, block: int, int_semantics: str = "reference"):
         self.kernel = kernel
+        self.int_semantics = int_semantics
         self.tensors = tensors          # name -> {"shape", "dtype"}
         self.args = args                # meta args by name
         self.grid = int(grid)
@@ -337,7 +338,8 @@ class Interpreter:
     def s_Assign(self, s, mask):
         dt = dtype_name(s.dtype) if s.dtype is not None else self.get(s.args[0])[1]
         vs = [self.get(a) for a in s.args]
-        v, rdt = op_on_values(s.op, [x for x, _ in vs], [d for _, d in vs], dt)
+        v, rdt = op_on_values(s.op, [x for x, _ in vs], [d for _, d in vs], dt,
+                              self.int_semantics)
         self.set(s.name, v, rdt, mask)
 
     def s_Let(self, s, mask):
@@ -588,17 +590,19 @@ def load_package(ir_path):
     return kernel, tensors, kmeta
 
 
-def run_package(ir_path, inputs: dict, out_init=None, scalars=None):
+def run_package(ir_path, inputs: dict, out_init=None, scalars=None,
+                int_semantics="reference"):
     """Run an IR package on host arrays; returns ``{output: array}``.
 
     ``out_init`` gives the initial contents of output buffers (default
     zeros) so that unwritten elements can be detected by the caller.
+    ``int_semantics`` as for the backend's Compiler option.
     """
     kernel, tensors, kmeta = load_package(ir_path)
     grid = _prod(kmeta.get("grid", [1]))
     block = _prod(kmeta.get("block", [1]))
     interp = Interpreter(kernel, tensors, {a["name"]: a for a in kmeta.get("args", [])},
-                         grid, block)
+                         grid, block, int_semantics)
     bufs = dict(inputs)
     for name in kernel.outputs:
         t = tensors[name]

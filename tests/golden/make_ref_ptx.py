@@ -3,7 +3,7 @@
 Run in a container that has the reference checkout (it is not needed, and not
 read, anywhere else):
 
-    python tests/golden/make_ref_ptx.py [--reference /path/to/emmy-ptx]
+    python tests/golden/make_ref_ptx.py --reference /path/to/emmy-ptx
 
 For each tag it writes ``problems/<tag>/`` (the IR package: ``*.ir.json`` +
 ``meta.json``, written by emmy_ptx.workloads) and ``problems/<tag>/ref.ptx``,
@@ -13,6 +13,7 @@ the reference compiler's PTX at its defaults (``.target sm_89``,
 """
 
 import argparse
+import os
 import importlib.util
 import subprocess
 import sys
@@ -37,7 +38,10 @@ def load_reference(root: Path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("EMMY_PTX_REFERENCE"),
+                    required="EMMY_PTX_REFERENCE" not in os.environ,
+                    help="root of the reference emmy-ptx checkout (or set "
+                         "EMMY_PTX_REFERENCE)")
     ap.add_argument("--tags", nargs="*", default=None)
     ap.add_argument("--no-ptxas", action="store_true")
     args = ap.parse_args()

@@ -30,6 +30,29 @@ def test_output_file_and_sidecar(tmp_path):
     assert side["entry"] == "k_rowsum_i32" and side["category"] == "rows"
 
 
+def test_output_file_goes_through_the_cache(tmp_path):
+    """``--cache-dir D -o out.ptx`` compiles into ``D/<key>.ptx`` (and the
+    sidecar into ``D/<key>.json``), as the reference routes ``-o`` through
+    compile_file (cli.py:50-66); a second run is a cache hit with identical
+    output and sidecar."""
+    from emmy_ptx.compiler import _cache_key
+    ir = _pkg(tmp_path)
+    cache = tmp_path / "cache"
+    args = [str(ir), "--target", "sm_100a", "--version", "8.7", "--cache-dir", str(cache)]
+    out1, out2 = tmp_path / "a.ptx", tmp_path / "b.ptx"
+    assert main(args + ["-o", str(out1)]) == 0
+    key = _cache_key(ir, "sm_100a", "8.7")
+    cached = cache / f"{key}.ptx"
+    assert cached.read_text() == out1.read_text()
+    assert (cache / f"{key}.json").exists()
+    # a cache hit: the cached PTX is served (mark it to prove it was read)
+    cached.write_text(cached.read_text() + "// cached\n")
+    assert main(args + ["-o", str(out2)]) == 0
+    assert out2.read_text() == cached.read_text()
+    assert (json.loads((tmp_path / "b.ptx.launch.json").read_text())
+            == json.loads((tmp_path / "a.ptx.launch.json").read_text()))
+
+
 def test_check(tmp_path, capsys):
     ir = _pkg(tmp_path)
     assert main([str(ir), "--target", "sm_100a", "--version", "8.7", "--check"]) == 0

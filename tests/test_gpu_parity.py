@@ -42,6 +42,29 @@ def test_sm100_kernel_matches_oracle(cuda, tag, geometry):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("tag", ["pointwise_i32_64x256", "pointwise_i32_33x100"])
+def test_torch_int_semantics_kernel_matches_oracle(cuda, tag):
+    """``int_semantics="torch"`` (floor division, divisor-signed remainder)
+    on the sm_100a pointwise kernel, bit for bit against the oracle's mode of
+    the same name (itself checked against torch on the CPU)."""
+    from emmy_ptx.runtime import Kernel
+    from oracle import simt
+    p = cases.problem(tag)
+    inputs = p.make_inputs()
+    assert (inputs["a"] < 0).any() and (inputs["b"] < 0).any()
+    with tempfile.TemporaryDirectory() as td:
+        ir_path = p.write(td)
+        kern = Kernel.from_ir(ir_path, int_semantics="torch")
+        got = run_on_gpu(kern, p, inputs, cuda)
+        want = simt.run_package(ir_path, inputs, out_init=output_init(p), int_semantics="torch")
+        trunc = simt.run_package(ir_path, inputs, out_init=output_init(p))
+    for o in p.outputs:
+        ok, msg = check_close(p.category, o, got[o], want[o], inputs)
+        assert ok, msg
+    assert (got["q"] != trunc["q"]).any(), "the torch mode changed nothing"
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("tag", list(cases.PARITY))
 def test_reference_ptx_matches_oracle(cuda, tag):
     """Oracle 1: the reference compiler's sm_89 PTX on the B200."""

@@ -181,3 +181,28 @@ def test_torch_cpu_baseline_matches_reference_gpu_vectors(tag):
     for o in p.outputs:
         ok, msg = check_close(p.category, o, got[o].numpy(), gold[o], inputs)
         assert ok, msg
+
+
+def test_torch_int_semantics_mode_is_torch_floor_division(tmp_path):
+    """The oracle's ``int_semantics="torch"`` mode (the backend option of the
+    same name) gives int32 floor_divide / remainder exactly torch's results,
+    negative operands included, while the default stays truncating."""
+    import torch
+    rng = np.random.default_rng(11)
+    a = rng.integers(-2**20, 2**20, 5000).astype(np.int32)
+    b = (rng.integers(1, 1000, 5000) * rng.choice([-1, 1], 5000)).astype(np.int32)
+    ta, tb = torch.from_numpy(a), torch.from_numpy(b)
+    q, _ = O.op_on_values("floor_divide", [a, b], ["s32", "s32"], "s32", "torch")
+    r, _ = O.op_on_values("remainder", [a, b], ["s32", "s32"], "s32", "torch")
+    assert (q == torch.floor_divide(ta, tb).numpy()).all()
+    assert (r == torch.remainder(ta, tb).numpy()).all()
+    qt, _ = O.op_on_values("floor_divide", [a, b], ["s32", "s32"], "s32")
+    assert (qt == torch.div(ta, tb, rounding_mode="trunc").numpy()).all()
+    assert (qt != q).any()
+    # the whole int32 package under the torch mode
+    p = cases.problem("pointwise_i32_33x100")
+    inputs = p.make_inputs()
+    got = simt.run_package(p.write(tmp_path), inputs, int_semantics="torch")
+    ta, tb = torch.from_numpy(inputs["a"]), torch.from_numpy(inputs["b"])
+    assert (got["q"].reshape(ta.shape) == torch.floor_divide(ta, tb).numpy()).all()
+    assert (got["r"].reshape(ta.shape) == torch.remainder(ta, tb).numpy()).all()
