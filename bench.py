@@ -44,6 +44,7 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "emmy-ptx_b200"))
 
+NVLINK_GBS = 770.0    # peer copy per direction per GPU, measured on this pool
 METRIC = "HBM GB/s (pointwise/norm) & TFLOP/s (matmul/attn) vs ref PTX, at 1/2/4/8 B200"
 HEADLINE = ("rmsnorm", "softmax")
 WORKLOAD = "config 2: RMSNorm [8192,4096] + row softmax [8192,32768], f32"
@@ -440,9 +441,10 @@ def config_block(world):
          "l2": "inputs larger than L2 (2.4 GB per step at N=1; at N>1 each rank's shard "
                "plus the 1.2 GB of gathered outputs)"}
     if world > 1:
-        c["exchange"] = ("each rank runs its 1/N of the rows of both kernels, then "
-                         "all_gather_into_tensor (NCCL) of both outputs into the full "
-                         "outputs on every rank, inside the timed step")
+        c["exchange"] = ("each rank runs its 1/N of the rows of both kernels; their "
+                         "epilogues store every output row into every rank's full output "
+                         "over NVLink (peer stores), then a one-element NCCL all-reduce "
+                         "marks completion, inside the timed step")
         c["parallelism"] = f"rows/{world}"
     return c
 
@@ -450,39 +452,64 @@ def config_block(world):
 class HeadlineStep:
     """The headline step on this rank.  N=1: the whole config.  N>1 (strong
     scaling): this rank's 1/N of the rows of every problem (each rank's rows
-    seeded on their own), then an NCCL all-gather of every output into the
-    full output, on the same stream."""
+    seeded on their own), and both full outputs on every rank at the end of
+    the step.  ``gather="fused"``: the row kernels' gather variant stores
+    every output row into every rank's full output over NVLink
+    (dist.FusedGather), then a one-element NCCL all-reduce on the stream
+    marks completion; ``gather="nccl"``: the plain kernels, then NCCL
+    all_gather_into_tensor of every output."""
 
-    def __init__(self, workdir, device, stream, rank, world):
+    def __init__(self, workdir, device, stream, rank, world, gather="fused"):
         import torch
+        from emmy_ptx import dist as edist
         from emmy_ptx import workloads
-        self.world, self.stream = world, stream
-        rows = {n: workloads.build(n).tensor(workloads.build(n).inputs[0])["shape"][0]
-                for n in HEADLINE}
+        self.world, self.stream, self.gather = world, stream, gather
+        rows = {n: edist.FULL_DEFAULTS[n]["rows"] for n in HEADLINE}
         self.bounds = [Bound(n, workdir, device, stream, seed_offset=rank,
                              rows=rows[n] // world if world > 1 else None) for n in HEADLINE]
         self.full_bytes = sum(workloads.build(n).algorithmic_bytes() for n in HEADLINE)
-        self.outs, self.gathered = [], []
-        if world > 1:
+        self.outs, self.gathered, self.fused = [], [], []
+        if world > 1 and gather == "nccl":
             for b in self.bounds:
                 for o in b.problem.outputs:
                     t = b.dev[o]
                     self.outs.append(t.reshape(-1))
                     self.gathered.append(torch.empty(world * t.numel(), dtype=t.dtype,
                                                      device=device))
+        elif world > 1:
+            for b in self.bounds:
+                fg = edist.FusedGather(b.problem.name, rank, world, workdir)
+                self.fused.append(fg.bind(b.dev, stream=stream))
+        # bytes each rank sends to its peers per step (fused: the row stores
+        # to the other ranks' outputs)
+        self.peer_bytes = [sum(int(b.dev[o].numel()) * b.dev[o].element_size()
+                               for o in b.problem.outputs) * (world - 1) for b in self.bounds]
+
+    @property
+    def kernels(self):
+        return [f.kernel for f in self.fused] if self.fused else [b.kernel for b in self.bounds]
 
     def launch_marked(self, marks=None):
         """Queue one step; record ``marks[i]`` after kernel i and the last
-        mark after the gathers."""
+        mark after the exchange."""
         import torch.distributed as dist
-        for i, b in enumerate(self.bounds):
-            b.launch()
+        launches = [f.launch for f in self.fused] if self.fused else \
+            [b.launch for b in self.bounds]
+        for i, launch in enumerate(launches):
+            launch()
             if marks is not None:
                 marks[i].record(self.stream)
+        if self.fused:
+            self.fused[-1].wait()        # every rank's kernels have finished
         for g, t in zip(self.gathered, self.outs):
             dist.all_gather_into_tensor(g, t)
         if marks is not None:
-            marks[len(self.bounds)].record(self.stream)
+            marks[len(launches)].record(self.stream)
+
+    def close(self):
+        for f in self.fused:
+            f.close()
+        self.fused = []
 
 
 def time_headline(hs, steps, warmup, barrier):
@@ -586,25 +613,54 @@ def run_b200(args):
     step_ms = max_over_ranks(step_ms)
     value = hs.full_bytes / step_ms / 1e6
 
-    # dominant kernel (largest share of the kernels' time): roofline
+    # dominant kernel (largest share of the kernels' time): roofline.  One
+    # GPU: HBM.  N>1: the gather kernels are bound by the bytes each rank
+    # must send to its peers over NVLink.
     j = max(range(len(bounds)), key=lambda i: per_kernel[i])
-    dom = bounds[j]
-    achieved = dom.bytes / per_kernel[j] / 1e6
-    roofline = {"kernel": dom.kernel.entry, "bound": "hbm", "achieved": round(achieved, 1),
-                "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / pk["hbm_gbs"], 4),
-                "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)"
-                if pk["source"] == "measured" else "fallback 6650 GB/s",
-                "algorithmic_bytes_per_launch": dom.bytes,
-                "ms_per_launch": round(per_kernel[j], 4)}
-    roofline.update(_traffic(dom.kernel.entry, dom.bytes))
-    kernels = {b.kernel.entry: {"ms": round(per_kernel[i], 4),
-                                "gbs": round(b.bytes / per_kernel[i] / 1e6, 1),
-                                "frac": round(b.bytes / per_kernel[i] / 1e6 / pk["hbm_gbs"], 4)}
-               for i, b in enumerate(bounds)}
+    dom, dk = bounds[j], hs.kernels[j]
+    if world == 1:
+        achieved = dom.bytes / per_kernel[j] / 1e6
+        roofline = {"kernel": dk.entry, "bound": "hbm", "achieved": round(achieved, 1),
+                    "peak": pk["hbm_gbs"], "unit": "GB/s",
+                    "frac": round(achieved / pk["hbm_gbs"], 4),
+                    "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)"
+                    if pk["source"] == "measured" else "fallback 6650 GB/s",
+                    "algorithmic_bytes_per_launch": dom.bytes,
+                    "ms_per_launch": round(per_kernel[j], 4)}
+        roofline.update(_traffic(dk.entry, dom.bytes))
+    else:
+        nv = hs.peer_bytes[j]
+        achieved = nv / max_over_ranks(per_kernel[j]) / 1e6
+        roofline = {"kernel": dk.entry + " (gather variant)", "bound": "nvlink",
+                    "achieved": round(achieved, 1), "peak": NVLINK_GBS, "unit": "GB/s",
+                    "frac": round(achieved / NVLINK_GBS, 4),
+                    "peak_source": "peer copy measured on this pool, per direction per GPU",
+                    "peer_bytes_per_launch": nv,
+                    "ms_per_launch": round(max_over_ranks(per_kernel[j]), 4), "traffic": None}
+    kernels = {k.entry: {"ms": round(per_kernel[i], 4),
+                         "gbs": round(b.bytes / per_kernel[i] / 1e6, 1),
+                         "frac": round(b.bytes / per_kernel[i] / 1e6 / pk["hbm_gbs"], 4)}
+               for i, (b, k) in enumerate(zip(bounds, hs.kernels))}
     hosts = [b.host for b in bounds] if world == 1 else None
     problems = [b.problem for b in bounds]
-    del bounds, hs
+    sharded = None
+    if world > 1:
+        # the same step with the plain kernels and NCCL all_gather_into_tensor
+        hs.close()
+        del bounds, hs
+        torch.cuda.empty_cache()
+        hn = HeadlineStep(workdir, device, stream, rank, world, gather="nccl")
+        n_ms, n_per, n_gather = time_headline(hn, max(3, args.steps // 2), 3, barrier)
+        kernel_only = max_over_ranks(sum(n_per))
+        sharded = {"config2": {
+            "fused_gather_incl_ms": round(step_ms, 4),
+            "nccl_gather_incl_ms": round(max_over_ranks(n_ms), 4),
+            "kernel_only_ms": round(kernel_only, 4),
+            "kernel_only_gbs": round(hn.full_bytes / kernel_only / 1e6, 1),
+            "partition": f"rows ({8192 // world} of 8192 per rank)"}}
+        del hn
+    else:
+        del bounds, hs
     torch.cuda.empty_cache()
 
     # end to end through the host-buffer API: each rank moves its own rows
@@ -625,14 +681,8 @@ def run_b200(args):
     link_total = sum(links)
     pcie_total = world * (e2e["h2d"] + e2e["d2h"]) / et / 1e6
 
-    sharded = None
     if world > 1:
         from emmy_ptx import dist as edist
-        sharded = {"config2_kernel_only": {
-            "ms": round(max_over_ranks(sum(per_kernel)), 4),
-            "gbs": round(sum(p.algorithmic_bytes() for p in problems) * world
-                         / max_over_ranks(sum(per_kernel)) / 1e6, 1),
-            "gather_ms": round(max_over_ranks(gather_ms), 4)}}
         # matmul 8192^3 in row blocks and causal attention 8x32x4096x128 in
         # (batch x head) pairs: NCCL all-gather vs the fused epilogue gather
         for name in ("matmul", "attention"):
@@ -668,7 +718,7 @@ def run_b200(args):
                         f"over {e2e['slots']} device slots on three C-ABI streams"},
     }
     if world > 1:
-        line["gather_ms_per_step"] = round(max_over_ranks(gather_ms), 4)
+        line["exchange_ms_per_step"] = round(max_over_ranks(gather_ms), 4)
     if sharded is not None:
         line["sharded"] = sharded
     if rank == 0 and world == 1:

@@ -274,22 +274,23 @@ class PeerBuffer:
 
 class FusedGather:
     """Rank ``rank``'s shard of ``name`` ("matmul": row blocks of C;
-    "attention": (batch x head) pairs of O) whose epilogue all-gathers the
-    output: after ``launch()`` and ``wait()`` on every rank, ``out`` holds
-    the full output on every rank.  ``bind`` takes the shard's buffers (its
-    own output buffer is not written)."""
+    "attention": (batch x head) pairs of O; "rmsnorm" / "softmax": row
+    blocks) whose epilogue all-gathers the output: after ``launch()`` and
+    ``wait()`` on every rank, ``out`` holds the full output on every rank.
+    ``bind`` takes the shard's buffers (its own output buffer is not
+    written)."""
 
     def __init__(self, name: str, rank: int, world: int, workdir, group=None, **kw):
         from .compiler import Compiler
         from .runtime import Kernel
-        from .sm100 import attention, matmul
-        if name not in ("matmul", "attention"):
+        from .sm100 import attention, matmul, rows
+        if name not in ("matmul", "attention", "rmsnorm", "softmax"):
             raise ValueError(f"no fused all-gather for {name}")
         self.name, self.rank, self.world, self.group = name, rank, world, group
         self.part, self.full = shard_problem(name, rank, world, **kw)
         ir = self.part.write(os.path.join(workdir, f"fused_{name}_{rank}"))
         comp = Compiler(ir, target="sm_100a", ptx_version="8.7")
-        mod = matmul if name == "matmul" else attention
+        mod = {"matmul": matmul, "attention": attention}.get(name, rows)
         ptx, side = mod.emit(comp, mod.match(comp), gather=world)
         geom = {"grid": comp.kmeta.get("grid") or [1], "block": comp.kmeta.get("block") or [1]}
         self.kernel = Kernel(ptx, comp.entry, Kernel._arg_specs(comp), geom, side)
@@ -297,6 +298,9 @@ class FusedGather:
         if name == "matmul":
             total = f["m"] * f["n"] * 4
             row0 = rank * self.part.tensor("A")["shape"][0]
+        elif name in ("rmsnorm", "softmax"):
+            total = f["rows"] * f["cols"] * 4
+            row0 = rank * self.part.tensor("x")["shape"][0]
         else:
             total = f["batch"] * f["heads"] * f["seq"] * f["head_dim"] * 4
             row0 = rank * self.part.tensor("q")["shape"][1] * f["seq"]

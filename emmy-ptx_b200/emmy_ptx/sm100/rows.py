@@ -395,7 +395,16 @@ def _warp_allreduce(b, op, dt, acc):
         _combine(b, op, dt, acc, o)
 
 
-def emit(comp, plan: RowPlan):
+def emit(comp, plan: RowPlan, gather: int = 0):
+    """``gather`` > 0: the all-gather variant for a row shard.  Instead of
+    writing ``out``, every output row is stored into up to ``gather``
+    full-size output buffers (this rank's and its peers', over NVLink) at
+    row ``emmy_gather_row0 + row``; the module globals ``emmy_gather_dst``
+    (``gather`` u64 pointers), ``emmy_gather_n`` (how many are used) and
+    ``emmy_gather_row0`` are set by the host before the first launch.
+    Plain stores only: no multicast, no waits on another GPU."""
+    if gather and (len(plan.row_outputs) != 1 or plan.scalar_outputs):
+        raise ValueError("the gather variant needs exactly one row output")
     b = KernelBuilder(comp.entry, comp.target, comp.ptx_version)
     T = plan.threads
     nw = T // 32
@@ -444,6 +453,10 @@ def emit(comp, plan: RowPlan):
     slot_bytes = 8
     nred = len(plan.reductions)
     b.module(f".shared .align 16 .b8 red_slots[{2 * nred * nw * slot_bytes}];")
+    if gather:
+        b.module(f".global .align 8 .b8 emmy_gather_dst[{8 * gather}];")
+        b.module(".global .align 4 .u32 emmy_gather_n;")
+        b.module(".global .align 4 .u32 emmy_gather_row0;")
     if prefetch:
         b.module(".shared .align 8 .b8 row_bar[8];")
         b.module(".shared .align 4 .u32 row_abort;")
@@ -497,6 +510,19 @@ def emit(comp, plan: RowPlan):
                 b.ins(f"{guard}ld.global{'.nc' if nc else ''}.v{len(rs)}.{mt} {{{', '.join(rs)}}}, {a};")
             else:
                 b.ins(f"{guard}st.global.v{len(rs)}.{mt} {a}, {{{', '.join(rs)}}};")
+
+    gdst, gpred, grow0 = [], [], None
+    if gather:
+        gn = b.reg("r")
+        grow0 = b.reg("r")
+        b.ins(f"ld.global.u32 {gn}, [emmy_gather_n];")
+        b.ins(f"ld.global.u32 {grow0}, [emmy_gather_row0];")
+        for d in range(gather):
+            gd, pd = b.reg("rd"), b.reg("p")
+            b.ins(f"ld.global.u64 {gd}, [emmy_gather_dst+{8 * d}];")
+            b.ins(f"setp.lt.u32 {pd}, {d}, {gn};")
+            gdst.append(gd)
+            gpred.append(pd)
 
     # broadcast vectors: loaded once, before the row loop
     vec_regs = {}
@@ -576,6 +602,14 @@ def emit(comp, plan: RowPlan):
         o = b.reg("rd")
         b.ins(f"mul.wide.u32 {o}, {row}, {C * nbytes(plan.dtypes[t])};")
         row_off[t] = o
+    gather_off = {}
+    if gather:
+        grow = b.reg("r")
+        b.ins(f"add.u32 {grow}, {grow0}, {row};")
+        for t in plan.row_outputs:
+            o = b.reg("rd")
+            b.ins(f"mul.wide.u32 {o}, {grow}, {C * nbytes(plan.dtypes[t])};")
+            gather_off[t] = o
     x_regs = {}
     if prefetch:
         dt = plan.dtypes[rt_]
@@ -721,7 +755,18 @@ def emit(comp, plan: RowPlan):
                     outs[t].append(reg)
             for t in plan.row_outputs:
                 dt = plan.dtypes[t]
-                vec_io(addr_of(ptrs[t], g, nbytes(dt), row_off[t]), dt, outs[t], False, valid[g])
+                if not gather:
+                    vec_io(addr_of(ptrs[t], g, nbytes(dt), row_off[t]), dt, outs[t], False,
+                           valid[g])
+                    continue
+                # the same vector into every destination's row row0 + row
+                for d in range(gather):
+                    pr_ = gpred[d]
+                    if valid[g]:
+                        pr_ = b.reg("p")
+                        b.ins(f"and.pred {pr_}, {gpred[d]}, {valid[g]};")
+                    vec_io(addr_of(gdst[d], g, nbytes(dt), gather_off[t]), dt, outs[t], False,
+                           pr_)
 
     b.ins(f"add.u32 {row}, {row}, {ncta};")
     b.ins(f"xor.b32 {parity}, {parity}, 1;")
@@ -742,4 +787,8 @@ def emit(comp, plan: RowPlan):
         "algorithmic_bytes": alg,
         "vectors_per_thread": G,
     }
+    if gather:
+        sidecar["gather"] = {"max_destinations": gather, "destinations": "emmy_gather_dst",
+                             "count": "emmy_gather_n", "row0": "emmy_gather_row0",
+                             "writes_out": False}
     return b.render(), sidecar

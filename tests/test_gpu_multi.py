@@ -12,7 +12,9 @@ import numpy as np
 import pytest
 
 KW = {"matmul": dict(m=512, n=384, k=256),
-      "attention": dict(batch=2, heads=2, seq=320, head_dim=64)}
+      "attention": dict(batch=2, heads=2, seq=320, head_dim=64),
+      "softmax": dict(rows=300, cols=32768),
+      "rmsnorm": dict(rows=64, cols=4096)}
 
 
 def _free_port():
@@ -77,6 +79,14 @@ def _worker(rank, world, port, out_dir, name):
 
 
 def _host_result(name, inputs, p):
+    if name == "softmax":
+        x = inputs["x"].astype(np.float64)
+        e = np.exp(x - x.max(1, keepdims=True))
+        return (e / e.sum(1, keepdims=True)).astype(np.float32)
+    if name == "rmsnorm":
+        x = inputs["x"].astype(np.float64)
+        return (x / np.sqrt((x * x).mean(1, keepdims=True) + p.params["eps"])
+                * inputs["w"]).astype(np.float32)
     if name == "matmul":
         return (inputs["A"].astype(np.float64) @ inputs["B"].astype(np.float64)).astype(np.float32)
     q, k, v = (inputs[n].astype(np.float64) for n in "qkv")
@@ -88,7 +98,7 @@ def _host_result(name, inputs, p):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("name", ["matmul", "attention"])
+@pytest.mark.parametrize("name", ["matmul", "attention", "softmax", "rmsnorm"])
 def test_fused_gather_on_two_gpus(tmp_path, name):
     import torch
     import torch.multiprocessing as mp
@@ -118,3 +128,50 @@ def test_fused_gather_on_two_gpus(tmp_path, name):
         for k in ("first", "second"):
             ok, msg = check_close(name, f"{name} rank {r} {k}", got[k], want, inputs)
             assert ok, msg
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,kw", [("softmax", dict(rows=296, cols=32768)),
+                                     ("softmax", dict(rows=6, cols=2052)),
+                                     ("rmsnorm", dict(rows=64, cols=4096))])
+def test_row_gather_epilogue_on_one_gpu(cuda, tmp_path, name, kw):
+    """The row kernels' gather variant, with two buffers of one GPU standing
+    in for two ranks' full outputs: rank 1's shard stores each row into both
+    at row ``row0 + row``, bit-identical to the regular kernel's row, and
+    leaves the other rank's rows and its own ``out`` argument untouched."""
+    import struct
+    import torch
+    from emmy_ptx import dist as edist
+    from emmy_ptx import workloads
+    from emmy_ptx.compiler import Compiler
+    from emmy_ptx.runtime import Kernel
+    from emmy_ptx.sm100 import rows
+    world, rank = 2, 1
+    full = workloads.build(name, **kw)
+    R, C = full.tensor("out")["shape"]
+    part, _ = edist.shard_problem(name, rank, world, **kw)
+    shard = edist.shard_inputs(name, full.make_inputs(), rank, world)
+    ir = part.write(tmp_path / "shard")
+    plain = Kernel.from_ir(ir)
+    comp = Compiler(ir, target="sm_100a", ptx_version="8.8")
+    ptx, side = rows.emit(comp, rows.match(comp), gather=world)
+    geom = {"grid": comp.kmeta.get("grid") or [1], "block": comp.kmeta.get("block") or [1]}
+    fused = Kernel(ptx, comp.entry, Kernel._arg_specs(comp), geom, side)
+    dev = {n: torch.from_numpy(v).to(cuda) for n, v in shard.items()}
+    ref = torch.full((R // world, C), float("nan"), device=cuda)
+    plain.launch({**dev, "out": ref})
+    dests = [torch.full((R, C), float("nan"), device=cuda) for _ in range(world)]
+    fused.set_global("emmy_gather_dst", struct.pack("<2Q", *(d.data_ptr() for d in dests)))
+    fused.set_global("emmy_gather_n", struct.pack("<I", world))
+    fused.set_global("emmy_gather_row0", struct.pack("<I", rank * (R // world)))
+    own = torch.full((R // world, C), float("nan"), device=cuda)
+    for _ in range(2):                                      # two calls in a row
+        for d in dests:
+            d.fill_(float("nan"))
+        fused.launch({**dev, "out": own})
+        torch.cuda.synchronize()
+        assert fused.status() == 0
+        for d in dests:
+            assert torch.equal(d[R // world:], ref), "gathered rows differ from the kernel's"
+            assert torch.isnan(d[:R // world]).all(), "wrote outside its rows"
+        assert torch.isnan(own).all(), "the gather variant wrote its own out argument"

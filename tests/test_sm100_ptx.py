@@ -159,3 +159,27 @@ def test_row_kernels_use_32_byte_vectors_from_isa_8_8(tmp_path):
     p = cases.problem("colreduce_f64_full")
     ptx = Compiler(p.write(tmp_path / "f64"), target="sm_100a", ptx_version="8.8").compile()
     assert ".v8." not in ptx
+
+
+@pytest.mark.parametrize("name,kw", [("softmax", dict(rows=1024, cols=32768)),
+                                     ("rmsnorm", dict(rows=1024, cols=4096)),
+                                     ("softmax", dict(rows=3, cols=2052))])
+def test_row_gather_variant_stores_to_every_destination(tmp_path, name, kw):
+    """The all-gather variant of the row kernels (an 8-rank shard) stores
+    each output vector once per destination from the table, never to its
+    own ``out`` argument, with plain stores only (no multicast), and
+    assembles without spills."""
+    from emmy_ptx import workloads
+    from emmy_ptx.sm100 import rows
+    p = workloads.build(name, **kw)
+    comp = Compiler(p.write(tmp_path), target="sm_100a", ptx_version="8.8")
+    plain = comp.compile()
+    ptx, side = rows.emit(comp, rows.match(comp), gather=8)
+    assert side["gather"]["max_destinations"] == 8
+    assert all(f"[emmy_gather_dst+{8 * d}]" in ptx for d in range(8))
+    n_st = lambda t: sum(1 for ln in t.splitlines() if ln.strip().lstrip("@!%p0123456789 ")  # noqa: E731
+                         .startswith("st.global"))
+    assert n_st(ptx) == 8 * n_st(plain)
+    assert MULTICAST not in ptx and "multimem" not in ptx
+    report = _build.ptxas_check(ptx)
+    assert "0 bytes spill stores" in report, report
