@@ -743,6 +743,7 @@ def _traffic(entry, algorithmic_bytes):
     f = ROOT / "profiles" / "traffic.json"
     try:
         rec = json.loads(f.read_text())[entry]
+        rec["dram_bytes_per_launch"], rec["algorithmic_bytes"], rec["summary"]
     except Exception:  # noqa: BLE001
         return {"traffic": None}
     t = rec["dram_bytes_per_launch"] * algorithmic_bytes / rec["algorithmic_bytes"]
