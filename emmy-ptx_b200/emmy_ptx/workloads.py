@@ -656,9 +656,12 @@ def matmul_fp8(m=8192, n=8192, k=8192, fmt="e4m3") -> Problem:
 
 
 # -- config 5: attention -----------------------------------------------------
-def attention(batch=8, heads=32, seq=4096, head_dim=128, causal=True, scale=None) -> Problem:
+def attention(batch=8, heads=32, seq=4096, head_dim=128, causal=True, scale=None,
+              block=384) -> Problem:
     """Causal self-attention, online softmax, one warp per query row; each
-    lane owns head_dim/32 dimensions of q and of the output accumulator."""
+    lane owns head_dim/32 dimensions of q and of the output accumulator.
+    Blocks of 12 warps (12 query rows per block in this per-row form; the
+    sm_100a kernel's 12 warps: softmax, producers and MMA, epilogue)."""
     assert head_dim % 32 == 0 and head_dim // 32 in (1, 2, 4)
     dpl = head_dim // 32
     scale = 1.0 / math.sqrt(head_dim) if scale is None else float(scale)
@@ -698,14 +701,14 @@ def attention(batch=8, heads=32, seq=4096, head_dim=128, causal=True, scale=None
             *[_assign(f"r__u{d}", "divide", (o[d], "l")) for d in range(dpl)],
             Write("out", qi, _names("r", dpl), F32, False, "NONE")]
     tile = Tile((Axis("b", Dim(batch)), Axis("h", Dim(heads)), Axis("i", Dim(seq)),
-                 Axis("dl", Dim(32))), tuple(body), block_threads=256)
+                 Axis("dl", Dim(32))), tuple(body), block_threads=block)
     name = "k_attention_causal" if causal else "k_attention"
     kop = KernelOp(name, ("q", "k", "v"), ("out",), (tile,))
     shape = (batch, heads, seq, head_dim)
     pairs = batch * heads * (seq * (seq + 1) // 2 if causal else seq * seq)
     return Problem("attention", "attention", kop,
                    [_t(n, shape, "f32") for n in ("q", "k", "v", "out")],
-                   _grid_for(batch * heads * seq * 32, 256), (256, 1, 1), seed=4,
+                   _grid_for(batch * heads * seq * 32, block), (block, 1, 1), seed=4,
                    params={"flops": 4 * pairs * head_dim, "scale": scale,
                            "causal": causal, "pairs": pairs})
 
