@@ -230,7 +230,9 @@ def link_gbs(device, nbytes=256 << 20, reps=3):
     """Host <-> device copy bandwidth with both directions in flight at once
     (pinned host buffers, one stream per direction, one cudaMemcpyAsync per
     copy): the ceiling of the end-to-end step, which moves its inputs in and
-    its outputs out over the same link.  Best of ``reps`` after a warm-up."""
+    its outputs out over the same link.  ``nbytes`` each way (the step's
+    own volume, so the ceiling is taken over as long a transfer); best of
+    ``reps`` after a warm-up."""
     import torch
     n = nbytes // 4
     h_in = torch.empty(n, dtype=torch.float32).pin_memory()
@@ -672,7 +674,7 @@ def run_b200(args):
     e2e_value = world * e2e["bytes"] / et / 1e6
     # every rank's link, both ways at once, all ranks copying together
     barrier()
-    mine = link_gbs(device)
+    mine = link_gbs(device, nbytes=max(e2e["h2d"], e2e["d2h"]) // 4 * 4)
     links = [mine]
     if world > 1:
         allv = [None] * world

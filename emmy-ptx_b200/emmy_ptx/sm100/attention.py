@@ -16,9 +16,9 @@ items are dealt by a static schedule computed at emit time (each item to
 the CTA whose items so far cost least) and stored in the module, so that
 causal items of 1 to S/128 key tiles leave no CTA with much more work than
 the others.  S = Q K^T is 3xTF32: Q hi K hi + Q hi K lo + Q lo K hi, where
-an operand's hi part is the operand itself (the tensor core reads an f32
-operand as tf32 by dropping its low 13 bits) and its lo part is the exact
-remainder.
+K's hi part is K itself (the tensor core reads an f32 operand as tf32 by
+dropping its low 13 bits) and a lo part is the exact remainder; Q is scaled
+by scale * log2(e) before its split, so scores come out in exp2 units.
 
 * a pre-pass entry (``<entry>_ksplit``) writes K's tf32 lo part and V
   rounded to the nearest tf32 value into scratch memory (each head's K and
@@ -27,29 +27,28 @@ remainder.
   product towards zero).
 * warps 0-3 (softmax): thread r owns query row r of the tile.  Per 128-key
   tile: ``tcgen05.ld`` of its 128 scores, the causal mask (diagonal tiles
-  only), tree max, lazy rescaling of the O accumulator in TMEM (only when
-  the row max grew by more than 2^8 in exp2 units), P = 2^((s - m) * scale *
-  log2 e) written over the scores in TMEM (the A operand of O += P V), tree
-  sum.  At the end of a work item the row sum goes to shared memory and the
-  warps go straight on to the next item's first tile.
+  only), max, lazy rescaling of the O accumulator in TMEM (only when the
+  row max grew by more than 2^8), P = 2^(s - m) written over the scores in
+  TMEM (the A operand of O += P V), tree sum.  At the end of a work item
+  the row sum goes to shared memory and the warps go straight on to the
+  next item's first tile.
 * warps 8-11 (epilogue): thread r of warp 8 + w owns query row 32w + r.
-  They stage the next item's Q -- loaded into registers early, written into
-  shared memory (the hi operand, K-major, 128-byte swizzle) once the current
-  item's last QK^T is complete, and its lo part into TMEM, one 32-dim chunk
-  at a time so the next QK^T can start on chunk 0 -- and then write the
-  finished item's output, O / l, after its last PV, releasing the O
+  They stage the next item's Q -- loaded into registers early, and once the
+  current item's last QK^T is complete split into tf32 hi (TMEM, the A
+  operand of two of the three products, so those read only K from shared
+  memory) and lo (shared memory, K-major, 128-byte swizzle), one 32-dim
+  chunk at a time so the next QK^T can start on chunk 0 -- and then write
+  the finished item's output, O / l, after its last PV, releasing the O
   accumulator to the next item's first PV as soon as they have read it.
-  So the change of work item costs the softmax and MMA warps almost nothing.
 * warps 4 and 6 (one thread each): TMA producers of K and V.  K arrives in
   chunks of 32 dims x 128 keys (a hi box and a lo box, K-major, 128-byte
   swizzle) through a 3-slot ring, each slot released after its part of
   QK^T; V in chunks of 64 keys (one box per 32 dims, N-major, 128-byte
   swizzle / 32-byte atoms) through a 2-slot ring, each released after its
   part of PV.
-* warp 5 (one thread): owns TMEM (512 columns: Q lo, O, two 128-column S/P
+* warp 5 (one thread): owns TMEM (512 columns: Q hi, O, two 128-column S/P
   buffers) and issues ``tcgen05.mma.kind::tf32`` with N = 128 for QK^T into
-  one S buffer while the softmax works on the other (Q from shared memory,
-  Q lo from TMEM).  At N = 64 an MMA measured 44 cycles against 32 of
+  one S buffer while the softmax works on the other.  At N = 64 an MMA measured 44 cycles against 32 of
   arithmetic; at N = 128 it runs at the arithmetic rate.
 * warp 7 (one thread): issues O += P V (P from TMEM).  An MMA instruction
   holds its issuing thread ~44 cycles, so two issuers keep the tensor core
@@ -83,6 +82,7 @@ REG_LAUNCH, REG_SOFTMAX, REG_PM, REG_EPI = 168, 216, 88, 200
 assert 128 * (REG_SOFTMAX + REG_PM + REG_EPI) <= THREADS * REG_LAUNCH
 LOG2E = 1.4426950408889634
 ROLE_SOFTMAX, ROLE_PRODUCER, ROLE_MMA, ROLE_EPILOGUE = 5, 6, 7, 8
+EPI_SLEEP_NS = 0   # nanosleep between the epilogue warps' polls (0: poll back to back)
 
 
 @dataclass
@@ -300,14 +300,14 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     KCH = 2 if gather else K_CHUNKS
     NVS = VS
     VPT = BKV // VC_KEYS               # V chunks per S tile
-    # shared memory: Q (the hi operand of Q K^T, itself: 128 rows, K-major,
+    # shared memory: Q lo (the A operand of Q lo K hi: 128 rows, K-major,
     # 128-byte swizzle, one 16 KB box per 32 dims) | K ring (a slot: 32 dims
     # of a 128-key chunk, hi box then lo box) | V ring (a slot: 64 keys, one
     # box per 32 dims) | barriers | row sums (two items) | gather stage
-    Q_RAW = 0
+    Q_LO = 0
     K_BOX = BKV * 128                  # 16 KB
     K_SLOT = 2 * K_BOX
-    K_RING = Q_RAW + BQ * D * 4
+    K_RING = Q_LO + BQ * D * 4
     V_BOX = VC_KEYS * 128              # 8 KB
     V_SLOT = DC * V_BOX
     V_RING = K_RING + KCH * K_SLOT
@@ -324,12 +324,14 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     EPI_WARP = 32 * EPI_ROW
     SMEM = EPI + (4 * EPI_WARP if gather else 0) + 1024
     assert SMEM <= 232448, SMEM
-    # TMEM columns: Q lo | O accumulator | S/P buffer 0 | S/P buffer 1
-    C_QLO, C_O, C_S0, C_S1 = 0, 128, 256, 384
+    # TMEM columns: Q hi | O accumulator | S/P buffer 0 | S/P buffer 1.  Q hi,
+    # the A operand of two of the three products, is read from TMEM, so an
+    # MMA of those reads only its K tile from shared memory.
+    C_QHI, C_O, C_S0, C_S1 = 0, 128, 256, 384
     VW = 8 if wide_vectors(comp.ptx_version) else 4    # floats per epilogue store
     TMEM_COLS = 512
     split_entry = comp.entry + "_ksplit"
-    qscale = plan.scale * LOG2E        # scores -> exp2 units, applied in the softmax
+    qscale = plan.scale * LOG2E        # folded into Q: scores come out in exp2 units
 
     b = KernelBuilder(comp.entry, comp.target, comp.ptx_version)
     b.module(".global .align 128 .b8 tmap_Khi[128];")
@@ -710,19 +712,19 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     b.ins(f"mov.u32 {id_s}, {idesc_tf32(BQ, BKV, False, False)};")
     ptrue, pfalse = preds()
     a_ = b.reg("r")
-    b.ins(f"add.u32 {a_}, {base}, {Q_RAW};")
+    b.ins(f"add.u32 {a_}, {base}, {Q_LO};")
     dq0 = desc(a_, kdesc)
-    dq = []                               # Q descriptor of k-step kk
+    dq = []                               # Q lo descriptor of k-step kk
     for kk in range(D // 8):
         c, w_ = divmod(kk, 4)
         r_ = b.reg("rd")
         b.ins(f"add.s64 {r_}, {dq0}, {(c * BQ * 128 + w_ * 32) >> 4};")
         dq.append(r_)
-    ql = []                               # Q lo TMEM address of k-step kk
+    qh = []                               # Q hi TMEM address of k-step kk
     for kk in range(D // 8):
         r_ = b.reg("r")
-        b.ins(f"add.u32 {r_}, {tmem}, {C_QLO + 8 * kk};")
-        ql.append(r_)
+        b.ins(f"add.u32 {r_}, {tmem}, {C_QHI + 8 * kk};")
+        qh.append(r_)
     a_ = b.reg("r")
     b.ins(f"add.u32 {a_}, {base}, {K_RING};")
     dk0 = desc(a_, kdesc)                 # K slot 0 (hi box; lo at + K_BOX)
@@ -764,12 +766,12 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
                     dh, dl = b.regs("rd", 2)
                     b.ins(f"add.s64 {dh}, {dk}, {(w_ * 32) >> 4};")
                     b.ins(f"add.s64 {dl}, {dk}, {(K_BOX + w_ * 32) >> 4};")
-                    # hi*hi and hi*lo with Q from shared memory, lo*hi with
-                    # Q lo from TMEM
-                    b.ins(f"{mma} [{ts}], {dq[kk]}, {dh}, {id_s}, "
+                    # hi*hi and hi*lo with Q hi from TMEM, lo*hi with Q lo
+                    # from shared memory
+                    b.ins(f"{mma} [{ts}], [{qh[kk]}], {dh}, {id_s}, "
                           f"{pfalse if kk == 0 else ptrue};")
-                    b.ins(f"{mma} [{ts}], {dq[kk]}, {dl}, {id_s}, {ptrue};")
-                    b.ins(f"{mma} [{ts}], [{ql[kk]}], {dh}, {id_s}, {ptrue};")
+                    b.ins(f"{mma} [{ts}], [{qh[kk]}], {dl}, {id_s}, {ptrue};")
+                    b.ins(f"{mma} [{ts}], {dq[kk]}, {dh}, {id_s}, {ptrue};")
                 tc.commit(bar_at("KE", ks))
                 advance(ks, kph, KCH)
             tc.commit(bar_at("SF", bi))
@@ -896,8 +898,6 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     t_x, it_x = b.regs("r", 2)
     b.ins(f"mov.u32 {t_x}, 0;")
     b.ins(f"mov.u32 {it_x}, 0;")
-    c_scale = f32_hex(qscale)
-    c_thr = f32_hex(8.0 / qscale)                    # 2^8 in exp2 units, in score units
 
     def soft_item(w, _kpos):
         bh, qt, qi, pq, rowoff = row_of(w, tid)
@@ -950,15 +950,14 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             mx = b.reg("f")
             b.ins(f"max.f32 {mx}, {tree(sv, 'max', chains=8)}, {m};")
             # lazy rescaling: keep the reference max unless the tile's max
-            # exceeds it by more than 2^8 in exp2 units (P stays below 256)
+            # exceeds it by more than 2^8 (P stays below 256)
             thr = b.reg("f")
-            b.ins(f"add.f32 {thr}, {m}, {c_thr};")
+            b.ins(f"add.f32 {thr}, {m}, 0f41000000;")
             need = b.reg("p")
             b.ins(f"setp.gt.f32 {need}, {mx}, {thr};")
             corr = b.reg("f")
             dm = b.reg("f")
             b.ins(f"sub.f32 {dm}, {m}, {mx};")
-            b.ins(f"mul.f32 {dm}, {dm}, {c_scale};")
             b.ins(f"ex2.approx.f32 {corr}, {dm};")
             pinf = b.reg("p")
             b.ins(f"setp.eq.f32 {pinf}, {m}, {ninf};")
@@ -991,12 +990,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             msub = b.reg("f")
             pm = b.reg("p")
             b.ins(f"setp.eq.f32 {pm}, {m}, {ninf};")
-            b.ins(f"mul.f32 {msub}, {m}, {c_scale};")
-            b.ins(f"selp.f32 {msub}, 0f00000000, {msub}, {pm};")
-            b.ins(f"neg.f32 {msub}, {msub};")
+            b.ins(f"selp.f32 {msub}, 0f00000000, {m}, {pm};")
             for e in range(BKV):
                 t_ = b.reg("f")
-                b.ins(f"fma.rn.f32 {t_}, {sv[e]}, {c_scale}, {msub};")
+                b.ins(f"sub.f32 {t_}, {sv[e]}, {msub};")
                 b.ins(f"ex2.approx.ftz.f32 {sv[e]}, {t_};")
                 # P as the tensor core will read it (tf32: low 13 bits
                 # dropped); the row sum below uses the same values, so
@@ -1037,7 +1034,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     b.ins(f"and.b32 {r8}, {etid}, 7;")
     qrow = b.reg("r")                               # this thread's row of Q in smem
     b.ins(f"mad.lo.u32 {qrow}, {etid}, 128, {base};")
-    b.ins(f"add.u32 {qrow}, {qrow}, {Q_RAW};")
+    b.ins(f"add.u32 {qrow}, {qrow}, {Q_LO};")
     lanes = D // 4
     pl_ = b.reg("p")
     b.ins(f"setp.lt.u32 {pl_}, {lane}, {lanes};")
@@ -1049,7 +1046,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     # smem address of (row wrow0 + i, box lc, unit lu): swizzle by row % 8
     qst = b.reg("r")
     b.ins(f"mad.lo.u32 {qst}, {lc}, {BQ * 128}, {base};")
-    b.ins(f"add.u32 {qst}, {qst}, {Q_RAW};")
+    b.ins(f"add.u32 {qst}, {qst}, {Q_LO};")
     b.ins(f"mad.lo.u32 {qst}, {wrow0}, 128, {qst};")
     if gather:
         # the destination pointers are read where they are used
@@ -1069,14 +1066,15 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         b.ins(f"mad.lo.u32 {st_w}, {lane}, {EPI_ROW}, {st_w};")
 
     def stage_q(w, wait_free):
-        """Q of item w: the warp loads its 32 rows coalesced (lane l: dims
-        4l..4l+3 of a row, 512 bytes per instruction) while the previous
-        item's QK^T still runs; once that is complete (QF) it writes them
-        into shared memory (the hi operand: row r of each 32-dim box, 16-byte
-        unit u at u ^ (r % 8), the K-major 128-byte-swizzle layout), and then
-        each thread reads its own row back, chunk by chunk, and writes the
-        exact remainder lo = q - (q with its low 13 bits cleared) into TMEM,
-        releasing the chunk to the QK^T issuer (QR[c])."""
+        """Q of item w into TMEM (hi) and shared memory (lo), chunk by chunk.
+        The warp loads its 32 rows coalesced (lane l: dims 4l..4l+3 of a row,
+        512 bytes per instruction) while the previous item's QK^T still
+        runs.  Once that is complete (QF) it writes them into the Q lo region
+        (row r of each 32-dim box, 16-byte unit u at u ^ (r % 8): the K-major
+        128-byte-swizzle layout); then each thread reads its own row back,
+        32 dims at a time, scales it by scale * log2(e) (scores come out in
+        exp2 units), splits it into tf32 hi (TMEM) and lo = x - hi (in
+        place), and releases the chunk to the QK^T issuer (QR[c])."""
         bh, qt, qi, pq, rowoff = row_of(w, etid)
         wb, t1, w1 = b.regs("rd", 3)
         b.ins(f"mul.wide.u32 {t1}, {etid}, {D * 4};")
@@ -1104,7 +1102,8 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             b.ins(f"@{pr_} ld.global.nc.v4.b32 {{{', '.join(v4)}}}, [{wb}+{i * D * 4}];")
             vals.append(v4)
         if wait_free is not None:
-            tc.wait(bar_at("QF"), wait_free, END, ROLE_EPILOGUE, uniform=True)
+            tc.wait(bar_at("QF"), wait_free, END, ROLE_EPILOGUE, uniform=True,
+                    sleep_ns=EPI_SLEEP_NS)
             b.ins("tcgen05.fence::after_thread_sync;")
         for i in range(32):
             ua = b.reg("r")
@@ -1112,32 +1111,40 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             b.ins(f"shl.b32 {ua}, {ua}, 4;")
             b.ins(f"add.u32 {ua}, {ua}, {qst};")
             b.ins(f"@{pl_} st.shared.v4.b32 [{ua}+{i * 128}], {{{', '.join(vals[i])}}};")
-        b.ins("fence.proxy.async.shared::cta;")       # Q, for the tensor core
         b.ins("bar.warp.sync 0xffffffff;")
         for c in range(DC):
-            x = []
+            x, addrs = [], []
             for u in range(8):
                 ua = b.reg("r")
                 b.ins(f"xor.b32 {ua}, {r8}, {u};")
                 b.ins(f"shl.b32 {ua}, {ua}, 4;")
                 b.ins(f"add.u32 {ua}, {ua}, {qrow};")
-                v4 = b.regs("r", 4)
-                b.ins(f"ld.shared.v4.b32 {{{', '.join(v4)}}}, [{ua}+{c * BQ * 128}];")
+                v4 = b.regs("f", 4)
+                b.ins(f"ld.shared.v4.f32 {{{', '.join(v4)}}}, [{ua}+{c * BQ * 128}];")
                 x += v4
+                addrs.append(ua)
+            hi = b.regs("r", 32)
             lo = b.regs("r", 32)
             for e in range(32):
-                # lo = q - hi exactly, hi = q with its low 13 bits cleared
-                # (what the tensor core reads).  A NaN or an infinity in Q
-                # reaches S through lo.
-                hb, hf, xf, lf = b.reg("r"), b.reg("f"), b.reg("f"), b.reg("f")
-                b.ins(f"and.b32 {hb}, {x[e]}, 0xFFFFE000;")
-                b.ins(f"mov.b32 {hf}, {hb};")
-                b.ins(f"mov.b32 {xf}, {x[e]};")
-                b.ins(f"sub.f32 {lf}, {xf}, {hf};")
+                # hi = x rounded to nearest tf32 (ties away) with two integer
+                # operations; lo = x - hi is exact.  A NaN or an infinity in
+                # Q still reaches S through lo.
+                b.ins(f"mul.f32 {x[e]}, {x[e]}, {f32_hex(qscale)};")
+                xb = b.reg("r")
+                b.ins(f"mov.b32 {xb}, {x[e]};")
+                b.ins(f"add.u32 {hi[e]}, {xb}, 4096;")
+                b.ins(f"and.b32 {hi[e]}, {hi[e]}, 0xFFFFE000;")
+                hf, lf = b.regs("f", 2)
+                b.ins(f"mov.b32 {hf}, {hi[e]};")
+                b.ins(f"sub.f32 {lf}, {x[e]}, {hf};")
                 b.ins(f"mov.b32 {lo[e]}, {lf};")
-            b.ins(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{ebase}+{C_QLO + 32 * c}], "
-                  f"{{{', '.join(lo)}}};")
+            b.ins(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{ebase}+{C_QHI + 32 * c}], "
+                  f"{{{', '.join(hi)}}};")
+            for u in range(8):
+                b.ins(f"st.shared.v4.b32 [{addrs[u]}+{c * BQ * 128}], "
+                      f"{{{', '.join(lo[4 * u:4 * u + 4])}}};")
             b.ins("tcgen05.wait::st.sync.aligned;")
+            b.ins("fence.proxy.async.shared::cta;")       # Q lo, for the tensor core
             b.ins("tcgen05.fence::before_thread_sync;")
             tc.arrive(bar_at("QR", c))
 
@@ -1150,8 +1157,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         hp = b.reg("r")
         b.ins(f"shr.u32 {hp}, {it_e}, 1;")
         b.ins(f"and.b32 {hp}, {hp}, 1;")
-        tc.wait(bar_at("LR", ib), hp, END, ROLE_EPILOGUE, uniform=True)
-        tc.wait(bar_at("OFIN"), parity(it_e), END, ROLE_EPILOGUE, uniform=True)
+        tc.wait(bar_at("LR", ib), hp, END, ROLE_EPILOGUE, uniform=True,
+                sleep_ns=EPI_SLEEP_NS)
+        tc.wait(bar_at("OFIN"), parity(it_e), END, ROLE_EPILOGUE, uniform=True,
+                sleep_ns=EPI_SLEEP_NS)
         b.ins("tcgen05.fence::after_thread_sync;")
         lb_ = b.reg("r")
         b.ins(f"mad.lo.u32 {lb_}, {ib}, {BQ * 4}, {base};")
