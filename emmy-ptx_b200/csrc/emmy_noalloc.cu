@@ -165,23 +165,6 @@ extern "C" int ert_attention_noalloc(uint64_t module, uint64_t attention_fn, uin
                     "it was compiled from",
                     heads_total, seq, head_dim, shape_name);
 
-    // The kernel's warpgroups re-divide their registers (setmaxnreg); the
-    // split assumes the register count per thread that the module names in
-    // emmy_launch_regs_<n>.  A kernel loaded with any other count could wait
-    // forever in that split, so it is not launched.
-    int regs = 0;
-    if (ert_function_attrs(attention_fn, &regs, nullptr, nullptr, nullptr) != 0)
-        return forward(err, err_len, ERT_E_ARGUMENT, "ert_function_attrs(attention)");
-    char regs_name[64];
-    snprintf(regs_name, sizeof regs_name, "emmy_launch_regs_%d", regs);
-    uint64_t regs_ptr = 0;
-    if (ert_module_global(module, regs_name, &regs_ptr, nullptr) != 0)
-        return fail(err, err_len, ERT_E_ARGUMENT,
-                    "ert_attention_noalloc: the attention kernel was loaded with %d registers "
-                    "per thread, not the count its register split assumes (no global %s); "
-                    "not launching it",
-                    regs, regs_name);
-
     void *scratch = nullptr;
     int rc = scratch_address(&scratch, err, err_len);
     if (rc) return rc;

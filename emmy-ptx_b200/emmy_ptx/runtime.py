@@ -322,17 +322,6 @@ class Kernel:
         self.sidecar = sidecar or {}
         self.module = Module(ptx)
         self.function = self.module.function(entry)
-        # a kernel whose warpgroups re-divide their registers (setmaxnreg)
-        # states the registers per thread its split assumes at launch; a
-        # split above the launch's registers would wait forever, so a
-        # different count from the JIT compiler is refused before any launch
-        want = self.sidecar.get("launch_registers")
-        if want is not None:
-            got = self.module.attrs(entry)["num_regs"]
-            if got != int(want):
-                raise EmmyRuntimeError(
-                    f"{entry}: loaded with {got} registers per thread, but its register "
-                    f"split assumes {want}; not launching it")
         self._tmap_cache: dict = {}
         self.launches = 0
         # scratch buffers the kernel needs beyond its arguments (sidecar

@@ -15,31 +15,24 @@ a few heads in L2), and inside a group the heaviest causal tiles first.  The
 items are dealt by a static schedule computed at emit time (each item to
 the CTA whose items so far cost least) and stored in the module, so that
 causal items of 1 to S/128 key tiles leave no CTA with much more work than
-the others.  S = Q K^T is 3xTF32: Q hi K hi + Q hi K lo + Q lo K hi, where
-K's hi part is K itself (the tensor core reads an f32 operand as tf32 by
-dropping its low 13 bits) and a lo part is the exact remainder; Q is scaled
-by scale * log2(e) before its split, so scores come out in exp2 units.
+the others:
 
-* a pre-pass entry (``<entry>_ksplit``) writes K's tf32 lo part and V
-  rounded to the nearest tf32 value into scratch memory (each head's K and
-  V are used by every query tile of the head, so doing this in the attention
-  kernel would repeat the work S/128 times; an unrounded V would bias every
-  product towards zero).
-* warps 0-3 (softmax): thread r owns query row r of the tile.  Per 128-key
-  tile: ``tcgen05.ld`` of its 128 scores, the causal mask (diagonal tiles
-  only), max, lazy rescaling of the O accumulator in TMEM (only when the
-  row max grew by more than 2^8), P = 2^(s - m) written over the scores in
-  TMEM (the A operand of O += P V), tree sum.  At the end of a work item
-  the row sum goes to shared memory and the warps go straight on to the
-  next item's first tile.
-* warps 8-11 (epilogue): thread r of warp 8 + w owns query row 32w + r.
-  They stage the next item's Q -- loaded into registers early, and once the
-  current item's last QK^T is complete split into tf32 hi (TMEM, the A
-  operand of two of the three products, so those read only K from shared
-  memory) and lo (shared memory, K-major, 128-byte swizzle), one 32-dim
-  chunk at a time so the next QK^T can start on chunk 0 -- and then write
-  the finished item's output, O / l, after its last PV, releasing the O
-  accumulator to the next item's first PV as soon as they have read it.
+* a pre-pass entry (``<entry>_ksplit``) writes K's tf32 lo part (K minus
+  K with its low 13 bits cleared; the kernel loads K itself as the hi part,
+  which the tensor core reads with those bits dropped) and V rounded to the
+  nearest tf32 value, into scratch memory (each head's K and V are used by
+  every query tile of the
+  head, so doing this in the attention kernel would repeat the work S/128
+  times; the tensor core drops the low 13 bits of an f32 operand, so an
+  unrounded V would bias every product towards zero).
+* warps 0-3 (softmax): thread r owns query row r of the tile.  It loads its
+  Q row, folds in scale * log2(e), splits it into tf32 hi/lo, stores hi into
+  TMEM and lo into shared memory (the A operands of S = Q K^T, which is
+  then in log2 units).  Per 128-key tile: ``tcgen05.ld`` of its 128
+  scores, the causal mask (diagonal tiles only), tree max, lazy rescaling
+  of the O accumulator in TMEM (only when the row max grew by more than
+  2^8), P = 2^(s - m) written over the scores in TMEM (the A operand of
+  O += P V), tree sum.
 * warps 4 and 6 (one thread each): TMA producers of K and V.  K arrives in
   chunks of 32 dims x 128 keys (a hi box and a lo box, K-major, 128-byte
   swizzle) through a 3-slot ring, each slot released after its part of
@@ -47,9 +40,11 @@ by scale * log2(e) before its split, so scores come out in exp2 units.
   swizzle / 32-byte atoms) through a 2-slot ring, each released after its
   part of PV.
 * warp 5 (one thread): owns TMEM (512 columns: Q hi, O, two 128-column S/P
-  buffers) and issues ``tcgen05.mma.kind::tf32`` with N = 128 for QK^T into
-  one S buffer while the softmax works on the other.  At N = 64 an MMA measured 44 cycles against 32 of
-  arithmetic; at N = 128 it runs at the arithmetic rate.
+  buffers) and issues ``tcgen05.mma.kind::tf32`` with N = 128:
+  S = Qhi Khi + Qhi Klo + Qlo Khi (3xTF32; Q hi from TMEM, Q lo from shared
+  memory) into one S buffer while the softmax works on the other.  At N = 64
+  an MMA measured 44 cycles against 32 of arithmetic; at N = 128 it runs at
+  the arithmetic rate.
 * warp 7 (one thread): issues O += P V (P from TMEM).  An MMA instruction
   holds its issuing thread ~44 cycles, so two issuers keep the tensor core
   busier than one; a barrier per S buffer orders QK^T(t+2) after PV(t).
@@ -71,18 +66,19 @@ from .tc import TC, idesc_tf32, smem_desc_hi, split_launch
 
 BQ = 128           # queries per tile (TMEM lanes)
 BKV = 128          # keys per S tile (the N of each QK^T MMA)
-BOX_KEYS = 64      # keys per TMA box, K and V alike
+BOX_KEYS = 64      # keys per TMA box, K and V alike (one shape for both kernels)
 VC_KEYS = 64       # keys per V chunk
-K_CHUNKS = 3       # K ring slots (2 with the gather stage)
-VS = 2             # V ring slots
-THREADS = 384      # 12 warps: softmax 0-3, producers/MMA 4-7, epilogue 8-11
-# registers per thread: at launch, and per warpgroup after setmaxnreg (the
-# shares sum to the launch's: 128 x (216 + 88 + 200) = 384 x 168)
-REG_LAUNCH, REG_SOFTMAX, REG_PM, REG_EPI = 168, 216, 88, 200
-assert 128 * (REG_SOFTMAX + REG_PM + REG_EPI) <= THREADS * REG_LAUNCH
+K_CHUNKS = 3       # one CTA per tile: K ring slots (2 with the gather stage)
+VS = 2             #                   V ring slots
+PAIR_K_CHUNKS = 6  # CTA pairs: K ring slots of half chunks (4 with the gather stage)
+PAIR_VS = 4        #            V ring slots of half chunks
+# CTA pairs (tcgen05 cta_group::2): correct and bit-identical to one CTA per
+# tile, but not faster at 8x32x4096x128 (3.77-3.98 against 3.78-3.79 ms on
+# one box): the doubled K/V lookahead removes the load waits, and an M=256
+# MMA then costs ~77 cycles per CTA against 64.  Off unless asked for.
+PAIR = False
 LOG2E = 1.4426950408889634
-ROLE_SOFTMAX, ROLE_PRODUCER, ROLE_MMA, ROLE_EPILOGUE = 5, 6, 7, 8
-EPI_SLEEP_NS = 0   # nanosleep between the epilogue warps' polls (0: poll back to back)
+ROLE_SOFTMAX, ROLE_PRODUCER, ROLE_MMA = 5, 6, 7
 
 
 @dataclass
@@ -158,8 +154,6 @@ def match(comp) -> AttnPlan:
     return AttnPlan(B, H, S, D, scale, causal, ins[0], ins[1], ins[2], outs[0])
 
 
-
-
 def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: int = 256) -> str:
     """The pre-pass entry ``entry(k, v, k_lo, v_r)``.  The tensor core reads
     an f32 operand as tf32 by dropping its low 13 bits, so the kernel loads
@@ -228,10 +222,9 @@ def head_group(bh: int) -> int:
 
 # items above this are dealt round-robin (the tables would bloat the module)
 SCHED_MAX_ITEMS = 16384
-# fixed cost of changing work item (the first K loads of a head, the wait
-# for the next Q) in eighths of a 128-key tile; the epilogue warps take the
-# output and the next Q off the critical path, leaving about one tile
-ITEM_COST_8THS = 8
+# fixed cost of changing work item (staging Q, the epilogue, the first K
+# loads of a head) in eighths of a 128-key tile, measured at ~2.4 tiles
+ITEM_COST_8THS = 19
 
 
 def item_schedule(costs, ncta):
@@ -254,26 +247,19 @@ def item_schedule(costs, ncta):
     return work, offs
 
 
+def pair_ok(comp, plan: AttnPlan) -> bool:
+    """CTA pairs split each K chunk by keys and each V chunk by head dims
+    (32-dim boxes, so head_dim 64 or 128), need two query tiles per head,
+    and an even grid under the meta.json geometry (a cluster of two)."""
+    g = comp.kmeta.get("grid") or [1]
+    g = [g] if isinstance(g, int) else list(g)
+    return (PAIR and plan.dim in (64, 128) and plan.seq > BQ and g[0] % 2 == 0)
+
 
 def shape_global(heads_total: int, seq: int, head_dim: int) -> str:
     """Name of the module global that records an attention module's compiled
     shape ((batch*heads) x keys x head_dim)."""
     return f"emmy_attn_shape_{heads_total}x{seq}x{head_dim}"
-
-
-def launch_regs_global(regs: int) -> str:
-    """Name of the module global that records the registers per thread the
-    kernel's register split assumes at launch."""
-    return f"emmy_launch_regs_{regs}"
-
-
-def _offsets(names_counts):
-    """Byte offsets of 8-byte mbarrier slots, in order."""
-    out, off = {}, 0
-    for name, n in names_counts:
-        out[name] = off
-        off += 8 * n
-    return out, off
 
 
 # ----------------------------------------------------------------------------
@@ -285,53 +271,57 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     ``emmy_gather_row0 + pair * seq + query`` of a [rows, head_dim] view:
     every rank's full output, peers' copies mapped over NVLink.
 
-    ``pair`` is accepted for callers of the earlier interface; only one
-    CTA per 128-query tile is built (a CTA-pair variant measured no faster)."""
-    if pair:
-        raise NoMatch("the attention kernel has no CTA-pair variant")
+    ``pair`` (default: ``pair_ok``): a cluster of two CTAs computes 256
+    query rows of one head with ``tcgen05.mma.cta_group::2`` (M=256).  Each
+    CTA owns 128 rows (its Q, S, P and O) and loads half of every K chunk
+    (64 of its 128 keys) and half of every V chunk (half of the head dims);
+    the even CTA issues every MMA.  Per CTA the K and V rings then hold
+    twice as many chunks in the same shared memory."""
     B, H, S, D = plan.batch, plan.heads, plan.seq, plan.dim
-    T = launch_block(comp) or THREADS
-    if T != THREADS:
-        raise NoMatch(f"the tcgen05 attention kernel needs {THREADS} threads per block "
-                      f"(meta.json has {T})")
+    if pair is None:
+        pair = pair_ok(comp, plan)
+    CG = 2 if pair else 1
+    T = launch_block(comp) or 256
+    if T != 256:
+        raise NoMatch(f"the tcgen05 attention kernel needs 256 threads per block (meta.json has {T})")
     DC = D // 32                       # 32-dim chunks
     nqt = -(-S // BQ)
-    items = B * H * nqt
-    KCH = 2 if gather else K_CHUNKS
-    NVS = VS
+    nqu = -(-nqt // CG)                # query units: tiles, or pairs of tiles
+    items = B * H * nqu
+    if pair:
+        KCH = 4 if gather else PAIR_K_CHUNKS
+        NVS = PAIR_VS
+    else:
+        KCH = 2 if gather else K_CHUNKS
+        NVS = VS
     VPT = BKV // VC_KEYS               # V chunks per S tile
-    # shared memory: Q lo (the A operand of Q lo K hi: 128 rows, K-major,
+    KC_KEYS = BKV // CG                # keys of a K chunk this CTA loads
+    VDC = DC // CG                     # 32-dim boxes of a V chunk this CTA loads
+    # shared memory: Q lo (the A operand of Qlo Khi: 128 rows, K-major,
     # 128-byte swizzle, one 16 KB box per 32 dims) | K ring (a slot: 32 dims
-    # of a 128-key chunk, hi box then lo box) | V ring (a slot: 64 keys, one
-    # box per 32 dims) | barriers | row sums (two items) | gather stage
+    # of this CTA's keys of a 128-key chunk, hi box then lo box) | V ring (a
+    # slot: 64 keys, one box per 32 of this CTA's dims) | barriers
     Q_LO = 0
-    K_BOX = BKV * 128                  # 16 KB
+    K_BOX = KC_KEYS * 128              # 16 KB (8 KB per CTA of a pair)
     K_SLOT = 2 * K_BOX
     K_RING = Q_LO + BQ * D * 4
     V_BOX = VC_KEYS * 128              # 8 KB
-    V_SLOT = DC * V_BOX
+    V_SLOT = VDC * V_BOX
     V_RING = K_RING + KCH * K_SLOT
     BAR = V_RING + NVS * V_SLOT
-    offs, nbar = _offsets([("KF", KCH), ("KE", KCH), ("VF", NVS), ("VE", NVS), ("QR", DC),
-                           ("QF", 1), ("SF", 2), ("PF", 2), ("OF", 1), ("OFIN", 1),
-                           ("DRAIN", 1), ("PE", 2), ("DRAIN2", 1), ("LR", 2), ("OR", 1)])
-    BAR_BYTES = nbar + 8               # + TMEM address slot and abort flag
-    LBUF = BAR + BAR_BYTES
-    # gather mode: a 32x32 transpose stage per epilogue warp (rows padded to
+    # gather mode: a 32x32 transpose stage per softmax warp (rows padded to
     # 144 B), so stores to peers are row-contiguous
-    EPI = LBUF + 2 * BQ * 4
+    BAR_BYTES = 320
+    EPI = BAR + BAR_BYTES
     EPI_ROW = 144
     EPI_WARP = 32 * EPI_ROW
     SMEM = EPI + (4 * EPI_WARP if gather else 0) + 1024
     assert SMEM <= 232448, SMEM
-    # TMEM columns: Q hi | O accumulator | S/P buffer 0 | S/P buffer 1.  Q hi,
-    # the A operand of two of the three products, is read from TMEM, so an
-    # MMA of those reads only its K tile from shared memory.
+    # TMEM columns: Q hi | O accumulator | S/P buffer 0 | S/P buffer 1
     C_QHI, C_O, C_S0, C_S1 = 0, 128, 256, 384
     VW = 8 if wide_vectors(comp.ptx_version) else 4    # floats per epilogue store
     TMEM_COLS = 512
     split_entry = comp.entry + "_ksplit"
-    qscale = plan.scale * LOG2E        # folded into Q: scores come out in exp2 units
 
     b = KernelBuilder(comp.entry, comp.target, comp.ptx_version)
     b.module(".global .align 128 .b8 tmap_Khi[128];")
@@ -341,18 +331,15 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     # tensor maps and scratch (libemmy_noalloc) looks this name up to refuse
     # a shape the module was not compiled for, with no device read
     b.module(f".visible .global .align 4 .u32 {shape_global(B * H, S, D)} = 1;")
-    # the register count per thread the setmaxnreg split below assumes at
-    # launch, also in a global's name: a launcher checks the loaded
-    # function's count against it before the first launch (a split larger
-    # than the launch's registers would wait forever)
-    b.module(f".visible .global .align 4 .u32 {launch_regs_global(REG_LAUNCH)} = 1;")
     b.module(".extern .shared .align 1024 .b8 dsmem[];")
     if gather:
         b.module(f".global .align 8 .b8 emmy_gather_dst[{8 * gather}];")
         b.module(".global .align 4 .u32 emmy_gather_n;")
         b.module(".global .align 4 .u32 emmy_gather_row0;")
     b.directive(f".maxntid {T}, 1, 1")
-    b.directive(f".maxnreg {REG_LAUNCH}")
+    if pair:
+        # launching without the cluster of two fails at launch time
+        b.directive(".reqnctapercluster 2, 1, 1")
     ptrs = declare_params(b, comp)
     pQ, pO = ptrs[plan.q], ptrs[plan.out]
 
@@ -366,23 +353,50 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     b.ins(f"and.b32 {base}, {base}, 0xFFFFFC00;")
     bars = b.reg("r")
     b.ins(f"add.u32 {bars}, {base}, {BAR};")
+    # barriers: K ring ([KCH]) and V ring ([NVS]), Q ready, S full / P full
+    # per S buffer, O (PV) done
+    KF, KE = 0, 8 * PAIR_K_CHUNKS
+    VF = 2 * 8 * PAIR_K_CHUNKS
+    VE = VF + 8 * PAIR_VS
+    QR = VE + 8 * PAIR_VS
+    SF, PF = QR + 8, QR + 24
+    # OF completes once per PV (the softmax waits on it only to rescale O,
+    # when the barrier is at most one phase past the awaited PV); OFIN once
+    # per work item, after its last PV -- the epilogue's wait.  A parity wait
+    # on OF there could see the barrier a phase *behind* the last PV and
+    # pass early.
+    OF, DRAIN, OFIN, FIN = QR + 40, QR + 48, QR + 56, QR + 64
+    # PE[b] completes when a PV that read the P in S buffer b is done (the
+    # QK^T issuer's wait before it overwrites the buffer); DRAIN2 is the PV
+    # issuer's own drain at teardown
+    PE, DRAIN2 = QR + 80, QR + 96
     slot, abort = b.regs("r", 2)
-    b.ins(f"add.u32 {slot}, {bars}, {nbar};")
-    b.ins(f"add.u32 {abort}, {bars}, {nbar + 4};")
-    tc = TC(b, abort, cta_group=1)
-    o_ = offs
+    b.ins(f"add.u32 {slot}, {bars}, {QR + 72};")
+    b.ins(f"add.u32 {abort}, {bars}, {QR + 76};")
+    assert DRAIN2 + 8 <= BAR_BYTES
+    tc = TC(b, abort, cta_group=CG)
 
     p = b.reg("p")
     skip = b.label("INIT_DONE")
     b.ins(f"setp.ne.u32 {p}, {tid}, 0;")
     b.ins(f"@{p} bra {skip};")
-    counts = {"KF": 1, "KE": 1, "VF": 1, "VE": 1, "QR": BQ, "QF": 1, "SF": 1, "PF": BQ,
-              "OF": 1, "OFIN": 1, "DRAIN": 1, "PE": 1, "DRAIN2": 1, "LR": BQ, "OR": BQ}
-    nslots = {"KF": KCH, "KE": KCH, "VF": NVS, "VE": NVS, "QR": DC, "SF": 2, "PF": 2, "PE": 2,
-              "LR": 2}
-    for name, off in o_.items():
-        for s in range(nslots.get(name, 1)):
-            tc.init(f"{bars}+{off + 8 * s}", counts[name])
+    for s in range(KCH):
+        for off in (KF, KE):
+            tc.init(f"{bars}+{off + 8 * s}", 1)
+    for s in range(NVS):
+        for off in (VF, VE):
+            tc.init(f"{bars}+{off + 8 * s}", 1)
+    tc.init(f"{bars}+{QR}", 128 * CG)         # every softmax thread of the pair
+    for k in range(2):
+        tc.init(f"{bars}+{SF + 8 * k}", 1)
+        tc.init(f"{bars}+{PF + 8 * k}", 128 * CG)
+    tc.init(f"{bars}+{OF}", 1)
+    tc.init(f"{bars}+{OFIN}", 1)
+    tc.init(f"{bars}+{DRAIN}", 1)
+    tc.init(f"{bars}+{FIN}", 1)
+    for k in range(2):
+        tc.init(f"{bars}+{PE + 8 * k}", 1)
+    tc.init(f"{bars}+{DRAIN2}", 1)
     b.ins(f"st.shared.u32 [{abort}], 0;")
     b.ins("fence.mbarrier_init.release.cluster;")
     b.place(skip)
@@ -392,20 +406,53 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     tc.tmem_alloc(slot, TMEM_COLS)
     b.place(skip2)
     b.ins("tcgen05.fence::before_thread_sync;")
-    b.ins(f"bar.sync 0, {T};")
+    if pair:
+        # both CTAs' barriers are initialised before either CTA's TMA bytes,
+        # MMA commits or arrivals can reach them
+        b.ins("barrier.cluster.arrive.release.aligned;")
+        b.ins("barrier.cluster.wait.acquire.aligned;")
+    else:
+        b.ins(f"bar.sync 0, {T};")
     b.ins("tcgen05.fence::after_thread_sync;")
     tmem = b.reg("r")
     b.ins(f"ld.shared.u32 {tmem}, [{slot}];")
-    cta, ncta = b.regs("r", 2)
-    b.ins(f"mov.u32 {cta}, %ctaid.x;")
-    b.ins(f"mov.u32 {ncta}, %nctaid.x;")
+    cta, ncta, rank = b.regs("r", 3)
+    lead = b.reg("p")                     # this CTA issues the MMAs
+    if pair:
+        # cta / ncta count CTA pairs; the leader is rank 0 of the cluster
+        b.ins(f"mov.u32 {cta}, %clusterid.x;")
+        b.ins(f"mov.u32 {ncta}, %nclusterid.x;")
+        b.ins(f"mov.u32 {rank}, %cluster_ctarank;")
+        lbars, pbars = b.regs("r", 2)     # the leader's and the peer's barrier blocks
+        b.ins(f"mapa.shared::cluster.u32 {lbars}, {bars}, 0;")
+        prk = b.reg("r")
+        b.ins(f"xor.b32 {prk}, {rank}, 1;")
+        b.ins(f"mapa.shared::cluster.u32 {pbars}, {bars}, {prk};")
+        tc.peer_abort = b.reg("r")
+        b.ins(f"add.u32 {tc.peer_abort}, {pbars}, {QR + 76};")
+    else:
+        b.ins(f"mov.u32 {cta}, %ctaid.x;")
+        b.ins(f"mov.u32 {ncta}, %nctaid.x;")
+        b.ins(f"mov.u32 {rank}, 0;")
+    b.ins(f"setp.eq.u32 {lead}, {rank}, 0;")
     END = b.label("END")
+
+    def remote(reg_base, off, s=None):
+        """shared::cluster address of barrier ``off`` (+ 8*s) in the
+        barrier block at ``reg_base`` (the leader's or the peer's)."""
+        r = b.reg("r")
+        if s is None:
+            b.ins(f"add.u32 {r}, {reg_base}, {off};")
+        else:
+            b.ins(f"mad.lo.u32 {r}, {s}, 8, {reg_base};")
+            b.ins(f"add.u32 {r}, {r}, {off};")
+        return r
 
     G = head_group(B * H)
 
-    # the item sequence of this CTA: a precomputed table when the launch has
-    # the grid the table was built for, else every ncta-th item
-    ncta_tab = min(items, 148)
+    # the item sequence of this CTA (or pair): a precomputed table when the
+    # launch has the grid the table was built for, else every ncta-th item
+    ncta_tab = min(items, 148 // CG)
     use_tab = b.reg("p")
     kbeg, kend, kstep = b.regs("r", 3)
     b.ins(f"mov.u32 {kbeg}, {cta};")
@@ -413,13 +460,13 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     b.ins(f"mov.u32 {kstep}, {ncta};")
     if items <= SCHED_MAX_ITEMS:
         def unit_cost(w):
-            qu = nqt - 1 - (w % (G * nqt)) // G
-            keys = min((qu + 1) * BQ, S) if plan.causal else S
+            qu = nqu - 1 - (w % (G * nqu)) // G
+            keys = min((qu + 1) * BQ * CG, S) if plan.causal else S
             return 8 * -(-keys // BKV) + ITEM_COST_8THS
-        work, offs_ = item_schedule([unit_cost(w) for w in range(items)], ncta_tab)
+        work, offs = item_schedule([unit_cost(w) for w in range(items)], ncta_tab)
         b.module(f".global .align 4 .u32 emmy_work[{items}] = {{{', '.join(map(str, work))}}};")
         b.module(f".global .align 4 .u32 emmy_work_off[{ncta_tab + 1}] = "
-                 f"{{{', '.join(map(str, offs_))}}};")
+                 f"{{{', '.join(map(str, offs))}}};")
         b.ins(f"setp.eq.u32 {use_tab}, {ncta}, {ncta_tab};")
         ta, to_ = b.reg("rd"), b.reg("rd")
         b.ins(f"mov.u64 {ta}, emmy_work_off;")
@@ -444,23 +491,33 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         return w
 
     def item_coords(w):
-        """Work item -> (bh, qt): heads in groups of G, and inside a group
-        the heaviest query tiles first.  CTAs that run at the same time then
-        read the K/V of a few heads, which stay in L2."""
-        bh, qt, g, r = b.regs("r", 4)
-        b.ins(f"div.u32 {g}, {w}, {G * nqt};")
-        b.ins(f"rem.u32 {r}, {w}, {G * nqt};")
-        b.ins(f"div.u32 {qt}, {r}, {G};")
-        b.ins(f"sub.u32 {qt}, {nqt - 1}, {qt};")
+        """Work item -> (bh, qu): heads in groups of G, and inside a group
+        the heaviest query units (a 128-query tile, or a pair of them)
+        first.  CTAs that run at the same time then read the K/V of a few
+        heads, which stay in L2."""
+        bh, qu, g, r = b.regs("r", 4)
+        b.ins(f"div.u32 {g}, {w}, {G * nqu};")
+        b.ins(f"rem.u32 {r}, {w}, {G * nqu};")
+        b.ins(f"div.u32 {qu}, {r}, {G};")
+        b.ins(f"sub.u32 {qu}, {nqu - 1}, {qu};")
         b.ins(f"rem.u32 {r}, {r}, {G};")
         b.ins(f"mad.lo.u32 {bh}, {g}, {G}, {r};")
-        return bh, qt
+        return bh, qu
 
-    def n_kv(qt):
-        """128-key tiles of query tile qt."""
+    def own_tile(qu):
+        """This CTA's 128-query tile of query unit qu."""
+        if not pair:
+            return qu
+        qt = b.reg("r")
+        b.ins(f"mad.lo.u32 {qt}, {qu}, 2, {rank};")
+        return qt
+
+    def n_kv(qu):
+        """128-key tiles of query unit qu (the pair's count for a pair: its
+        lower tile's last key tile is then fully masked)."""
         n = b.reg("r")
         if plan.causal:
-            b.ins(f"mad.lo.u32 {n}, {qt}, {BQ}, {BQ};")
+            b.ins(f"mad.lo.u32 {n}, {qu}, {BQ * CG}, {BQ * CG};")
             b.ins(f"min.u32 {n}, {n}, {S};")
             b.ins(f"add.u32 {n}, {n}, {BKV - 1};")
             b.ins(f"div.u32 {n}, {n}, {BKV};")
@@ -510,13 +567,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         b.ins(f"and.b32 {ph}, {ph}, 1;")
         return s, ph
 
-    def bar_at(name, s=None):
-        off = o_[name]
+    def bar_at(off, s=None):
         r = b.reg("r")
         if s is None:
             b.ins(f"add.u32 {r}, {bars}, {off};")
-        elif isinstance(s, int):
-            b.ins(f"add.u32 {r}, {bars}, {off + 8 * s};")
         else:
             b.ins(f"mad.lo.u32 {r}, {s}, 8, {bars};")
             b.ins(f"add.u32 {r}, {r}, {off};")
@@ -529,33 +583,11 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             b.ins(f"xor.b32 {r}, {r}, 1;")
         return r
 
-    def skip_unless(pred, label):
-        """Branch past a block unless ``pred`` holds; returns the label to
-        place after the block."""
-        lb = b.label(label)
-        b.ins(f"@!{pred} bra.uni {lb};")
-        return lb
-
     roles = [b.label("SOFTMAX"), b.label("PRODUCER_K"), b.label("MMA_QK"), b.label("PRODUCER_V"),
-             b.label("MMA_PV"), b.label("EPILOGUE")]
+             b.label("MMA_PV")]
     pr = b.reg("p")
-    # register split per warpgroup (each warpgroup is one kind of role):
-    # the producer/MMA warpgroup gives registers back, the softmax and
-    # epilogue warpgroups take theirs; the shares add up to the launch's
-    # 384 x REG_LAUNCH.  Each warpgroup adjusts right before its own roles,
-    # so the code of a role is reached from one register budget only.
-    wg1, wg2 = b.label("WG_PM"), b.label("WG_EPI")
-    b.ins(f"setp.ge.u32 {pr}, {warp}, 8;")
-    b.ins(f"@{pr} bra {wg2};")
-    b.ins(f"setp.ge.u32 {pr}, {warp}, 4;")
-    b.ins(f"@{pr} bra {wg1};")
-    b.ins(f"setmaxnreg.inc.sync.aligned.u32 {REG_SOFTMAX};")
-    b.ins(f"bra.uni {roles[0]};")
-    b.place(wg2)
-    b.ins(f"setmaxnreg.inc.sync.aligned.u32 {REG_EPI};")
-    b.ins(f"bra.uni {roles[5]};")
-    b.place(wg1)
-    b.ins(f"setmaxnreg.dec.sync.aligned.u32 {REG_PM};")
+    b.ins(f"setp.lt.u32 {pr}, {warp}, 4;")
+    b.ins(f"@{pr} bra {roles[0]};")
     b.ins(f"setp.eq.u32 {pr}, {warp}, 4;")
     b.ins(f"@{pr} bra {roles[1]};")
     b.ins(f"setp.eq.u32 {pr}, {warp}, 5;")
@@ -577,36 +609,52 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             b.ins(f"prefetch.tensormap [{tm}];")
         return maps
 
-    # K: per S tile, DC chunks (32 dims of 128 keys, hi and lo; boxes of 64 keys)
+    def full_barrier(off, s, nbytes):
+        """Announce ``nbytes`` on full barrier off[s] (the leader does, for
+        both CTAs of a pair) and return the barrier this CTA's TMA bytes
+        count on (the leader's)."""
+        if not pair:
+            fb = bar_at(off, s)
+            tc.arrive_expect_tx(fb, nbytes)
+            return fb
+        sk = b.label("EXPECTED")
+        b.ins(f"@!{lead} bra {sk};")
+        tc.arrive_expect_tx(bar_at(off, s), CG * nbytes)
+        b.place(sk)
+        return remote(lbars, off, s)
+
+    # K: per S tile, DC chunks (32 dims of 128 keys: this CTA's keys, hi and
+    # lo; boxes of 64 keys)
     tmKh, tmKl = producer_start(roles[1], ("tmap_Khi", "tmap_Klo"))
     t_kp = b.reg("r")
     b.ins(f"mov.u32 {t_kp}, 0;")
 
     def prod_k_item(w, _k):
-        bh, qt = item_coords(w)
-        nkv = n_kv(qt)
+        bh, qu = item_coords(w)
+        nkv = n_kv(qu)
 
         def tile(j):
             k0 = b.reg("r")
             b.ins(f"mul.lo.u32 {k0}, {j}, {BKV};")
+            if pair:
+                b.ins(f"mad.lo.u32 {k0}, {rank}, {KC_KEYS}, {k0};")
             for c in range(DC):
                 s, ph = ring(t_kp, KCH)
                 flip = b.reg("r")
                 b.ins(f"xor.b32 {flip}, {ph}, 1;")
-                tc.wait(bar_at("KE", s), flip, END, ROLE_PRODUCER)
-                fb = bar_at("KF", s)
-                tc.arrive_expect_tx(fb, K_SLOT)
+                tc.wait(bar_at(KE, s), flip, END, ROLE_PRODUCER)
+                fb = full_barrier(KF, s, K_SLOT)
                 dst = b.reg("r")
                 b.ins(f"mad.lo.u32 {dst}, {s}, {K_SLOT}, {base};")
                 b.ins(f"add.u32 {dst}, {dst}, {K_RING};")
                 x = b.reg("r")
                 b.ins(f"mov.u32 {x}, {32 * c};")
                 for half, tm in ((0, tmKh), (K_BOX, tmKl)):
-                    for kb in range(BKV // BOX_KEYS):
+                    for kb in range(KC_KEYS // BOX_KEYS):
                         y, d = b.regs("r", 2)
                         b.ins(f"add.u32 {y}, {k0}, {kb * BOX_KEYS};")
                         b.ins(f"add.u32 {d}, {dst}, {half + kb * BOX_KEYS * 128};")
-                        tc.tma_load_3d(d, tm, x, y, bh, fb)
+                        tc.tma_load_3d(d, tm, x, y, bh, fb, pair)
                 b.ins(f"add.u32 {t_kp}, {t_kp}, 1;")
         kv_loop(nkv, tile, None, "PKKV")
 
@@ -619,27 +667,28 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     b.ins(f"mov.u32 {t_vp}, 0;")
 
     def prod_v_item(w, _k):
-        bh, qt = item_coords(w)
-        nkv = n_kv(qt)
+        bh, qu = item_coords(w)
+        nkv = n_kv(qu)
+        x0 = b.reg("r")                   # this CTA's first head dim
+        b.ins(f"mul.lo.u32 {x0}, {rank}, {32 * VDC};")
 
         def tile(j):
             for v in range(VPT):
                 s, ph = ring(t_vp, NVS)
                 flip = b.reg("r")
                 b.ins(f"xor.b32 {flip}, {ph}, 1;")
-                tc.wait(bar_at("VE", s), flip, END, ROLE_PRODUCER)
-                fb = bar_at("VF", s)
-                tc.arrive_expect_tx(fb, V_SLOT)
+                tc.wait(bar_at(VE, s), flip, END, ROLE_PRODUCER)
+                fb = full_barrier(VF, s, V_SLOT)
                 dst = b.reg("r")
                 b.ins(f"mad.lo.u32 {dst}, {s}, {V_SLOT}, {base};")
                 b.ins(f"add.u32 {dst}, {dst}, {V_RING};")
                 k0 = b.reg("r")
                 b.ins(f"mad.lo.u32 {k0}, {j}, {BKV}, {v * VC_KEYS};")
-                for c in range(DC):
+                for c in range(VDC):
                     x, a_ = b.regs("r", 2)
-                    b.ins(f"mov.u32 {x}, {32 * c};")
+                    b.ins(f"add.u32 {x}, {x0}, {32 * c};")
                     b.ins(f"add.u32 {a_}, {dst}, {c * V_BOX};")
-                    tc.tma_load_3d(a_, tmV, x, k0, bh, fb)
+                    tc.tma_load_3d(a_, tmV, x, k0, bh, fb, pair)
                 b.ins(f"add.u32 {t_vp}, {t_vp}, 1;")
         kv_loop(nkv, tile, None, "PVKV")
 
@@ -660,9 +709,17 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         b.place(label)
         b.ins(f"setp.ne.u32 {pr}, {lane}, 0;")
         b.ins(f"@{pr} bra {END};")
+        b.ins(f"@!{lead} bra {END};")         # the pair's MMAs are the leader's
 
-    mma = "tcgen05.mma.cta_group::1.kind::tf32"
-    kdesc = smem_desc_hi(16, 8 * 128, "128B")                  # K, Q: K-major rows of 128 B
+    mma = f"tcgen05.mma.cta_group::{CG}.kind::tf32"
+
+    def release(off, s=None):
+        """Commit to barrier off(+8s) of this CTA and, in a pair, of the
+        peer (the same completed MMAs free or fill both CTAs' buffers)."""
+        tc.commit(bar_at(off, s))
+        if pair:
+            tc.commit(remote(pbars, off, s))
+    kdesc = smem_desc_hi(16, 8 * 128, "128B")                  # K, Q lo: K-major rows of 128 B
     vdesc = smem_desc_hi(V_BOX, 4 * 128, "128B_base32B")       # V: N-major, 32-dim box stride
 
     def preds():
@@ -680,12 +737,12 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         b.ins(f"or.b64 {d}, {d}, 0x{const:016X};")
         return d
 
-    def advance(slot_, ph, n):
+    def advance(slot, ph, n):
         """Ring slot and phase parity of the next use (no division)."""
         pw = b.reg("p")
-        b.ins(f"add.u32 {slot_}, {slot_}, 1;")
-        b.ins(f"setp.eq.u32 {pw}, {slot_}, {n};")
-        b.ins(f"@{pw} mov.u32 {slot_}, 0;")
+        b.ins(f"add.u32 {slot}, {slot}, 1;")
+        b.ins(f"setp.eq.u32 {pw}, {slot}, {n};")
+        b.ins(f"@{pw} mov.u32 {slot}, 0;")
         b.ins(f"@{pw} xor.b32 {ph}, {ph}, 1;")
 
     def s_col(tg):
@@ -703,22 +760,20 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         return bi, ph
 
     # -- QK^T issuer (warp 5).  Everything an MMA needs that does not change
-    # from tile to tile is computed once: Q descriptors, Q lo TMEM addresses,
-    # the K ring's base descriptor.  An item's first tile waits, per 32-dim
-    # chunk, for that chunk of Q (QR); after its last tile a commit (QF)
-    # tells the epilogue warps that Q's buffers are free for the next item.
+    # from tile to tile is computed once: Q lo descriptors, Q hi TMEM
+    # addresses, the K ring's base descriptor.
     mma_role(roles[2])
     id_s = b.reg("r")
-    b.ins(f"mov.u32 {id_s}, {idesc_tf32(BQ, BKV, False, False)};")
+    b.ins(f"mov.u32 {id_s}, {idesc_tf32(BQ * CG, BKV, False, False)};")
     ptrue, pfalse = preds()
     a_ = b.reg("r")
     b.ins(f"add.u32 {a_}, {base}, {Q_LO};")
-    dq0 = desc(a_, kdesc)
+    dqlo = desc(a_, kdesc)
     dq = []                               # Q lo descriptor of k-step kk
     for kk in range(D // 8):
         c, w_ = divmod(kk, 4)
         r_ = b.reg("rd")
-        b.ins(f"add.s64 {r_}, {dq0}, {(c * BQ * 128 + w_ * 32) >> 4};")
+        b.ins(f"add.s64 {r_}, {dqlo}, {(c * BQ * 128 + w_ * 32) >> 4};")
         dq.append(r_)
     qh = []                               # Q hi TMEM address of k-step kk
     for kk in range(D // 8):
@@ -733,16 +788,12 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         b.ins(f"mov.u32 {r_}, 0;")
 
     def qk_item(w, _k):
-        bh, qt = item_coords(w)
-        nkv = n_kv(qt)
-        itp = parity(it_m)
-        last = b.reg("r")
-        b.ins(f"sub.u32 {last}, {nkv}, 1;")
+        bh, qu = item_coords(w)
+        nkv = n_kv(qu)
+        tc.wait(bar_at(QR), parity(it_m), END, ROLE_MMA)
+        b.ins("tcgen05.fence::after_thread_sync;")
 
         def tile(j):
-            pfirst, plast = b.regs("p", 2)
-            b.ins(f"setp.eq.u32 {pfirst}, {j}, 0;")
-            b.ins(f"setp.eq.u32 {plast}, {j}, {last};")
             # S buffer t%2 is free once PV(t-2), which read its P, is done
             bi, ph = buf_phase(t_m)
             p2 = b.reg("p")
@@ -750,14 +801,12 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             b.ins(f"setp.lt.u32 {p2}, {t_m}, 2;")
             b.ins(f"@{p2} bra.uni {free};")
             b.ins(f"xor.b32 {ph}, {ph}, 1;")
-            tc.wait(bar_at("PE", bi), ph, END, ROLE_MMA)
+            tc.wait(bar_at(PE, bi), ph, END, ROLE_MMA)
+            b.ins("tcgen05.fence::after_thread_sync;")
             b.place(free)
             ts = s_col(t_m)
             for c in range(DC):
-                tc.wait(bar_at("KF", ks), kph, END, ROLE_MMA)
-                lb = skip_unless(pfirst, "Q_READY")
-                tc.wait(bar_at("QR", c), itp, END, ROLE_MMA)
-                b.place(lb)
+                tc.wait(bar_at(KF, ks), kph, END, ROLE_MMA)
                 b.ins("tcgen05.fence::after_thread_sync;")
                 dk = b.reg("rd")
                 b.ins(f"mad.wide.u32 {dk}, {ks}, {K_SLOT >> 4}, {dk0};")
@@ -772,12 +821,9 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
                           f"{pfalse if kk == 0 else ptrue};")
                     b.ins(f"{mma} [{ts}], [{qh[kk]}], {dl}, {id_s}, {ptrue};")
                     b.ins(f"{mma} [{ts}], {dq[kk]}, {dh}, {id_s}, {ptrue};")
-                tc.commit(bar_at("KE", ks))
+                release(KE, ks)
                 advance(ks, kph, KCH)
-            tc.commit(bar_at("SF", bi))
-            lb = skip_unless(plast, "Q_FREE")
-            tc.commit(bar_at("QF"))
-            b.place(lb)
+            release(SF, bi)
         kv_loop(nkv, tile, t_m, "MKV")
         b.ins(f"add.u32 {it_m}, {it_m}, 1;")
     item_loop(qk_item, "MIT")
@@ -786,24 +832,22 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     # -- PV issuer (warp 7): O += P V for every S tile, VPT chunks of 64 keys,
     # each released (VE) as soon as its MMAs are done; then OF (per tile),
     # PE (the S buffer is free again) and, after an item's last tile, OFIN.
-    # An item's first PV overwrites O, so it waits until the epilogue warps
-    # have read the previous item's O (OR).
     mma_role(roles[4])
     id_o = b.reg("r")
-    b.ins(f"mov.u32 {id_o}, {idesc_tf32(BQ, D, False, True)};")
+    b.ins(f"mov.u32 {id_o}, {idesc_tf32(BQ * CG, D, False, True)};")
     ptrue, _ = preds()
     a_ = b.reg("r")
     b.ins(f"add.u32 {a_}, {base}, {V_RING};")
     dv0 = desc(a_, vdesc)                 # V slot 0
     to = b.reg("r")
     b.ins(f"add.u32 {to}, {tmem}, {C_O};")
-    vs, vph, t_p, it_p = b.regs("r", 4)   # V ring slot and parity, S tiles, items
-    for r_ in (vs, vph, t_p, it_p):
+    vs, vph, t_p = b.regs("r", 3)         # V ring slot and parity, S tiles
+    for r_ in (vs, vph, t_p):
         b.ins(f"mov.u32 {r_}, 0;")
 
     def pv_item(w, _k):
-        bh, qt = item_coords(w)
-        nkv = n_kv(qt)
+        bh, qu = item_coords(w)
+        nkv = n_kv(qu)
         t0 = b.reg("r")
         b.ins(f"mov.u32 {t0}, {t_p};")
 
@@ -811,21 +855,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             first_pred = b.reg("p")       # accumulate after the item's first tile
             b.ins(f"setp.ne.u32 {first_pred}, {t_p}, {t0};")
             bi, ph = buf_phase(t_p)
-            tc.wait(bar_at("PF", bi), ph, END, ROLE_MMA)
-            # the item's first PV: the previous item's O has been read
-            pw = b.reg("p")
-            b.ins(f"setp.eq.u32 {pw}, {t_p}, {t0};")
-            pn = b.reg("p")
-            b.ins(f"setp.ne.u32 {pn}, {it_p}, 0;")
-            b.ins(f"and.pred {pw}, {pw}, {pn};")
-            lb = skip_unless(pw, "O_READ")
-            prev = b.reg("r")
-            b.ins(f"sub.u32 {prev}, {it_p}, 1;")
-            tc.wait(bar_at("OR"), parity(prev), END, ROLE_MMA)
-            b.place(lb)
+            tc.wait(bar_at(PF, bi), ph, END, ROLE_MMA)
             sc = s_col(t_p)
             for v in range(VPT):
-                tc.wait(bar_at("VF", vs), vph, END, ROLE_MMA)
+                tc.wait(bar_at(VF, vs), vph, END, ROLE_MMA)
                 b.ins("tcgen05.fence::after_thread_sync;")
                 dv = b.reg("rd")
                 b.ins(f"mad.wide.u32 {dv}, {vs}, {V_SLOT >> 4}, {dv0};")
@@ -836,33 +869,47 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
                     b.ins(f"add.u32 {pa}, {sc}, {v * VC_KEYS + 8 * kk};")
                     b.ins(f"{mma} [{to}], [{pa}], {dvk}, {id_o}, "
                           f"{first_pred if v == 0 and kk == 0 else ptrue};")
-                tc.commit(bar_at("VE", vs))
+                release(VE, vs)
                 advance(vs, vph, NVS)
-            tc.commit(bar_at("OF"))
-            tc.commit(bar_at("PE", bi))
+            release(OF)
+            tc.commit(bar_at(PE, bi))     # only this CTA's QK^T issuer waits on it
         kv_loop(nkv, tile, t_p, "PKV")
-        tc.commit(bar_at("OFIN"))
-        b.ins(f"add.u32 {it_p}, {it_p}, 1;")
+        release(OFIN)
     item_loop(pv_item, "PIT")
     b.ins(f"bra.uni {END};")
 
+    # ---- softmax / lazy correction / epilogue ------------------------------------
+    b.place(roles[0])
+    q4 = b.reg("r")
+    b.ins(f"shl.b32 {q4}, {warp}, 21;")              # (32*warp) << 16: TMEM lane base
+    lbase = b.reg("r")
+    b.ins(f"add.u32 {lbase}, {tmem}, {q4};")
+    t_x, it_x = b.regs("r", 2)
+    b.ins(f"mov.u32 {t_x}, 0;")
+    b.ins(f"mov.u32 {it_x}, 0;")
+    qscale = plan.scale * LOG2E
+    if gather:
+        # the destination pointers are read where they are used (the
+        # softmax's 128 scores per thread leave no registers to hold them)
+        gn, grow0 = b.regs("r", 2)
+        b.ins(f"ld.global.u32 {gn}, [emmy_gather_n];")
+        b.ins(f"ld.global.u32 {grow0}, [emmy_gather_row0];")
+        # this warp's stage: written at row = lane, read at row lane/8 (+4i),
+        # 16-byte column chunk lane%8
+        st_w, st_r, sub_row, sub_col = b.regs("r", 4)
+        b.ins(f"mad.lo.u32 {st_w}, {warp}, {EPI_WARP}, {base};")
+        b.ins(f"add.u32 {st_w}, {st_w}, {EPI};")
+        b.ins(f"shr.u32 {sub_row}, {lane}, 3;")
+        b.ins(f"and.b32 {sub_col}, {lane}, 7;")
+        b.ins(f"mad.lo.u32 {st_r}, {sub_row}, {EPI_ROW}, {st_w};")
+        b.ins(f"mad.lo.u32 {st_r}, {sub_col}, 16, {st_r};")
+        b.ins(f"shl.b32 {sub_col}, {sub_col}, 2;")
+        b.ins(f"mad.lo.u32 {st_w}, {lane}, {EPI_ROW}, {st_w};")
     ninf = "0fFF800000"
 
-    def tree(vals, op, chains=0):
-        """Pairwise reduction (log depth) of registers ``vals``.  With
-        ``chains``, first fold the values into that many running results
-        (so the inputs, still needed afterwards, and the partial results are
-        not all live at once), then reduce those pairwise."""
+    def tree(vals, op):
+        """Pairwise reduction (log depth) of registers ``vals``."""
         vals = list(vals)
-        if chains and len(vals) > chains:
-            acc = []
-            for i in range(chains):
-                r = b.reg("f")
-                b.ins(f"{op}.f32 {r}, {vals[i]}, {vals[i + chains]};")
-                for k in range(i + 2 * chains, len(vals), chains):
-                    b.ins(f"{op}.f32 {r}, {r}, {vals[k]};")
-                acc.append(r)
-            vals = acc
         while len(vals) > 1:
             nxt = []
             for i in range(0, len(vals) - 1, 2):
@@ -874,12 +921,21 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             vals = nxt
         return vals[0]
 
-    def row_of(w, row):
-        """Item w and tile row ``row``: (bh, qt, query index, in range?, row
-        byte offset)."""
-        bh, qt = item_coords(w)
-        qi = b.reg("r")
-        b.ins(f"mad.lo.u32 {qi}, {qt}, {BQ}, {row};")
+    def to_leader(off, s=None):
+        """Arrive on barrier off(+8s) of the MMA-issuing CTA: this CTA's,
+        or the pair leader's."""
+        if pair:
+            tc.arrive_cluster(remote(lbars, off, s))
+        else:
+            tc.arrive(bar_at(off, s))
+
+    def row_of(w):
+        """Item w: (bh, query unit, this CTA's query tile, this thread's
+        query, in range?, row byte offset)."""
+        bh, qu = item_coords(w)
+        qt = own_tile(qu)
+        qi = b.reg("r")                          # this thread's query index
+        b.ins(f"mad.lo.u32 {qi}, {qt}, {BQ}, {tid};")
         pq = b.reg("p")
         b.ins(f"setp.lt.u32 {pq}, {qi}, {S};")
         rowoff = b.reg("rd")
@@ -887,24 +943,149 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         qo = b.reg("rd")
         b.ins(f"mul.wide.u32 {qo}, {qi}, {D * 4};")
         b.ins(f"add.s64 {rowoff}, {rowoff}, {qo};")
-        return bh, qt, qi, pq, rowoff
+        return bh, qu, qt, qi, pq, rowoff
 
-    # ---- softmax (warps 0-3) -------------------------------------------------------
-    b.place(roles[0])
-    q4 = b.reg("r")
-    b.ins(f"shl.b32 {q4}, {warp}, 21;")              # (32*warp) << 16: TMEM lane base
-    lbase = b.reg("r")
-    b.ins(f"add.u32 {lbase}, {tmem}, {q4};")
-    t_x, it_x = b.regs("r", 2)
-    b.ins(f"mov.u32 {t_x}, 0;")
-    b.ins(f"mov.u32 {it_x}, 0;")
+    def stage_q(w):
+        """Q of item w into TMEM (hi) and shared memory (lo), then Q ready.
+        Called for the next item as soon as the current item's last QK^T
+        is complete (its S tile has been seen), so the QK^T issuer can start
+        the next item while this item's epilogue runs."""
+        bh, qu, qt, qi, pq, rowoff = row_of(w)
+        # Q * scale * log2(e) -> tf32 hi (TMEM) and lo (shared memory): scores
+        # come out in log2 units.  Row r of Q lo goes to row r of each 32-dim
+        # box with the 128-byte swizzle (16-byte unit u at u ^ (r % 8)), the
+        # layout the K-major smem descriptor describes.
+        qrow = b.reg("r")
+        b.ins(f"mad.lo.u32 {qrow}, {tid}, 128, {base};")
+        b.ins(f"add.u32 {qrow}, {qrow}, {Q_LO};")
+        r8 = b.reg("r")
+        b.ins(f"and.b32 {r8}, {tid}, 7;")
+        # 1. the warp loads its 32 rows coalesced (lane l: dims 4l..4l+3 of
+        #    a row, 512 bytes per instruction) into the Q lo region, in the
+        #    swizzled layout (32-dim box c = l / 8, 16-byte unit u = l % 8)
+        wrow0 = b.reg("r")                      # the warp's first row
+        b.ins(f"and.b32 {wrow0}, {tid}, 0xFFFFFFE0;")
+        lanes = D // 4
+        pl_ = b.reg("p")
+        b.ins(f"setp.lt.u32 {pl_}, {lane}, {lanes};")
+        lc, lu = b.regs("r", 2)
+        b.ins(f"shr.u32 {lc}, {lane}, 3;")
+        b.ins(f"and.b32 {lu}, {lane}, 7;")
+        # global address of (the warp's first row, dim 4 * lane):
+        # rowoff is this thread's row, so subtract tid rows, add wrow0 rows
+        wb, t1, w1 = b.regs("rd", 3)
+        b.ins(f"mul.wide.u32 {t1}, {tid}, {D * 4};")
+        b.ins(f"mul.wide.u32 {w1}, {wrow0}, {D * 4};")
+        b.ins(f"sub.s64 {wb}, {rowoff}, {t1};")
+        b.ins(f"add.s64 {wb}, {wb}, {w1};")
+        loff = b.reg("rd")
+        b.ins(f"mul.wide.u32 {loff}, {lane}, 16;")
+        b.ins(f"add.s64 {wb}, {wb}, {loff};")
+        b.ins(f"add.s64 {wb}, {wb}, {pQ};")
+        # the warp's first row within the sequence (qi - tid + wrow0); rows
+        # at or past S (a partial last query tile) are not loaded
+        qrow0 = b.reg("r")
+        b.ins(f"sub.u32 {qrow0}, {qi}, {tid};")
+        b.ins(f"add.u32 {qrow0}, {qrow0}, {wrow0};")
+        vals = []
+        for i in range(32):
+            v4 = b.regs("r", 4)
+            for e in range(4):
+                b.ins(f"mov.b32 {v4[e]}, 0;")
+            rr = b.reg("r")
+            b.ins(f"add.u32 {rr}, {qrow0}, {i};")
+            pr_ = b.reg("p")
+            b.ins(f"setp.lt.and.u32 {pr_}, {rr}, {S}, {pl_};")
+            b.ins(f"@{pr_} ld.global.nc.v4.b32 {{{', '.join(v4)}}}, [{wb}+{i * D * 4}];")
+            vals.append(v4)
+        # smem address of (row wrow0 + i, box lc, unit lu): swizzle by row % 8
+        sbase = b.reg("r")
+        b.ins(f"mad.lo.u32 {sbase}, {lc}, {BQ * 128}, {base};")
+        b.ins(f"add.u32 {sbase}, {sbase}, {Q_LO};")
+        b.ins(f"mad.lo.u32 {sbase}, {wrow0}, 128, {sbase};")
+        pst = b.reg("p")
+        b.ins(f"setp.lt.u32 {pst}, {lane}, {lanes};")
+        for i in range(32):
+            ua = b.reg("r")
+            b.ins(f"xor.b32 {ua}, {lu}, {i % 8};")
+            b.ins(f"shl.b32 {ua}, {ua}, 4;")
+            b.ins(f"add.u32 {ua}, {ua}, {sbase};")
+            b.ins(f"@{pst} st.shared.v4.b32 [{ua}+{i * 128}], {{{', '.join(vals[i])}}};")
+        b.ins("bar.warp.sync 0xffffffff;")
+        # 2. each thread reads its own row back, splits it, writes lo in place
+        for c in range(DC):
+            raw = []
+            addrs = []
+            for u in range(8):
+                ua = b.reg("r")
+                b.ins(f"xor.b32 {ua}, {r8}, {u};")
+                b.ins(f"shl.b32 {ua}, {ua}, 4;")
+                b.ins(f"add.u32 {ua}, {ua}, {qrow};")
+                v4 = b.regs("f", 4)
+                b.ins(f"ld.shared.v4.f32 {{{', '.join(v4)}}}, [{ua}+{c * BQ * 128}];")
+                raw += v4
+                addrs.append(ua)
+            x = raw
+            hi = b.regs("r", 32)
+            lo = b.regs("r", 32)
+            for e in range(32):
+                # hi = x rounded to nearest tf32 (ties away), as two integer
+                # operations (cvt.rna is several times dearer here, on the
+                # path between items); lo = x - hi is exact.  A NaN or an
+                # infinity in Q still reaches S through lo, as with cvt.rna.
+                b.ins(f"mul.f32 {x[e]}, {x[e]}, {f32_hex(qscale)};")
+                xb = b.reg("r")
+                b.ins(f"mov.b32 {xb}, {x[e]};")
+                b.ins(f"add.u32 {hi[e]}, {xb}, 4096;")
+                b.ins(f"and.b32 {hi[e]}, {hi[e]}, 0xFFFFE000;")
+                hf, lf = b.regs("f", 2)
+                b.ins(f"mov.b32 {hf}, {hi[e]};")
+                b.ins(f"sub.f32 {lf}, {x[e]}, {hf};")
+                b.ins(f"mov.b32 {lo[e]}, {lf};")
+            b.ins(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{lbase}+{C_QHI + 32 * c}], "
+                  f"{{{', '.join(hi)}}};")
+            for u in range(8):
+                b.ins(f"st.shared.v4.b32 [{addrs[u]}+{c * BQ * 128}], "
+                      f"{{{', '.join(lo[4 * u:4 * u + 4])}}};")
+        b.ins("tcgen05.wait::st.sync.aligned;")
+        b.ins("fence.proxy.async.shared::cta;")           # Q lo, for the tensor core
+        b.ins("tcgen05.fence::before_thread_sync;")
+        to_leader(QR)
 
-    def soft_item(w, _kpos):
-        bh, qt, qi, pq, rowoff = row_of(w, tid)
-        nkv = n_kv(qt)
+    def prefetch_q(w):
+        """One thread asks L2 for item w's Q block (128 contiguous rows),
+        an item ahead of its staging, so the staging loads hit L2."""
+        bh, qu = item_coords(w)
+        qt = own_tile(qu)
+        r0, nrow = b.regs("r", 2)
+        b.ins(f"mad.lo.u32 {r0}, {bh}, {S}, 0;")
+        b.ins(f"mad.lo.u32 {r0}, {qt}, {BQ}, {r0};")
+        b.ins(f"mul.lo.u32 {nrow}, {qt}, {BQ};")
+        b.ins(f"sub.u32 {nrow}, {S}, {nrow};")
+        b.ins(f"min.u32 {nrow}, {nrow}, {BQ};")
+        b.ins(f"mul.lo.u32 {nrow}, {nrow}, {D * 4};")
+        qa = b.reg("rd")
+        b.ins(f"mul.wide.u32 {qa}, {r0}, {D * 4};")
+        b.ins(f"add.s64 {qa}, {qa}, {pQ};")
+        b.ins(f"cp.async.bulk.prefetch.L2.global [{qa}], {nrow};")
+
+    def soft_item(w, kpos):
+        bh, qu, qt, qi, pq, rowoff = row_of(w)
+        nkv = n_kv(qu)
+        kn = b.reg("r")                   # the next item's position
+        b.ins(f"add.u32 {kn}, {kpos}, {kstep};")
+        pp = b.reg("p")
+        nopf = b.label("NO_Q_PREFETCH")
+        b.ins(f"setp.ge.u32 {pp}, {kn}, {kend};")
+        b.ins(f"@{pp} bra.uni {nopf};")
+        b.ins(f"setp.ne.u32 {pp}, {tid}, 0;")
+        b.ins(f"@{pp} bra {nopf};")
+        prefetch_q(item_at(kn))
+        b.place(nopf)
+        b.ins("bar.warp.sync 0xffffffff;")
         qfirst = b.reg("r")                      # the item's first query
         b.ins(f"mul.lo.u32 {qfirst}, {qt}, {BQ};")
-        m, l_ = b.regs("f", 2)            # m: the max P is scaled by (score units)
+        m, l_ = b.regs("f", 2)            # m: the max P is scaled by (log2 units)
         b.ins(f"mov.f32 {m}, {ninf};")
         b.ins(f"mov.f32 {l_}, 0f00000000;")
         t0 = b.reg("r")
@@ -912,7 +1093,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
 
         def tile(j):
             bi, ph = buf_phase(t_x)
-            tc.wait(bar_at("SF", bi), ph, END, ROLE_SOFTMAX, uniform=True)
+            tc.wait(bar_at(SF, bi), ph, END, ROLE_SOFTMAX, uniform=True)
             b.ins("tcgen05.fence::after_thread_sync;")
             scol = b.reg("r")
             b.ins(f"mad.lo.u32 {scol}, {bi}, {C_S1 - C_S0}, {lbase};")
@@ -948,7 +1129,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
                 b.ins(f"selp.f32 {sv[e]}, {sv[e]}, {ninf}, {pc};")
             b.place(nomask)
             mx = b.reg("f")
-            b.ins(f"max.f32 {mx}, {tree(sv, 'max', chains=8)}, {m};")
+            b.ins(f"max.f32 {mx}, {tree(sv, 'max')}, {m};")
             # lazy rescaling: keep the reference max unless the tile's max
             # exceeds it by more than 2^8 (P stays below 256)
             thr = b.reg("f")
@@ -972,7 +1153,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             b.ins(f"@!{pany} bra.uni {no_rs};")
             prev = b.reg("r")
             b.ins(f"sub.u32 {prev}, {t_x}, 1;")
-            tc.wait(bar_at("OF"), parity(prev), END, ROLE_SOFTMAX, uniform=True)
+            tc.wait(bar_at(OF), parity(prev), END, ROLE_SOFTMAX, uniform=True)
             b.ins("tcgen05.fence::after_thread_sync;")
             for c in range(DC):
                 ov = b.regs("f", 32)
@@ -1005,193 +1186,40 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             b.ins(f"add.f32 {l_}, {l_}, {tree(sv, 'add')};")
             b.ins("tcgen05.wait::st.sync.aligned;")
             b.ins("tcgen05.fence::before_thread_sync;")
-            tc.arrive(bar_at("PF", bi))
+            to_leader(PF, bi)
         kv_loop(nkv, tile, t_x, "XKV")
-        # the item's row sum, for the epilogue warps (two items' slots)
-        lb_ = b.reg("r")
-        ib = b.reg("r")
-        b.ins(f"and.b32 {ib}, {it_x}, 1;")
-        b.ins(f"mad.lo.u32 {lb_}, {ib}, {BQ * 4}, {base};")
-        b.ins(f"mad.lo.u32 {lb_}, {tid}, 4, {lb_};")
-        b.ins(f"st.shared.f32 [{lb_}+{LBUF}], {l_};")
-        tc.arrive(bar_at("LR", ib))
-        b.ins(f"add.u32 {it_x}, {it_x}, 1;")
-    item_loop(soft_item, "XIT")
-    b.ins(f"bra.uni {END};")
-
-    # ---- epilogue (warps 8-11): the next item's Q, then this item's output -------
-    b.place(roles[5])
-    ew, etid = b.regs("r", 2)
-    b.ins(f"sub.u32 {ew}, {warp}, 8;")
-    b.ins(f"sub.u32 {etid}, {tid}, 256;")           # the tile row this thread owns
-    e4 = b.reg("r")
-    b.ins(f"shl.b32 {e4}, {ew}, 21;")
-    ebase = b.reg("r")
-    b.ins(f"add.u32 {ebase}, {tmem}, {e4};")
-    it_e = b.reg("r")
-    b.ins(f"mov.u32 {it_e}, 0;")
-    r8 = b.reg("r")
-    b.ins(f"and.b32 {r8}, {etid}, 7;")
-    qrow = b.reg("r")                               # this thread's row of Q in smem
-    b.ins(f"mad.lo.u32 {qrow}, {etid}, 128, {base};")
-    b.ins(f"add.u32 {qrow}, {qrow}, {Q_LO};")
-    lanes = D // 4
-    pl_ = b.reg("p")
-    b.ins(f"setp.lt.u32 {pl_}, {lane}, {lanes};")
-    lc, lu = b.regs("r", 2)
-    b.ins(f"shr.u32 {lc}, {lane}, 3;")
-    b.ins(f"and.b32 {lu}, {lane}, 7;")
-    wrow0 = b.reg("r")                              # the warp's first tile row
-    b.ins(f"shl.b32 {wrow0}, {ew}, 5;")
-    # smem address of (row wrow0 + i, box lc, unit lu): swizzle by row % 8
-    qst = b.reg("r")
-    b.ins(f"mad.lo.u32 {qst}, {lc}, {BQ * 128}, {base};")
-    b.ins(f"add.u32 {qst}, {qst}, {Q_LO};")
-    b.ins(f"mad.lo.u32 {qst}, {wrow0}, 128, {qst};")
-    if gather:
-        # the destination pointers are read where they are used
-        gn, grow0 = b.regs("r", 2)
-        b.ins(f"ld.global.u32 {gn}, [emmy_gather_n];")
-        b.ins(f"ld.global.u32 {grow0}, [emmy_gather_row0];")
-        # this warp's stage: written at row = lane, read at row lane/8 (+4i),
-        # 16-byte column chunk lane%8
-        st_w, st_r, sub_row, sub_col = b.regs("r", 4)
-        b.ins(f"mad.lo.u32 {st_w}, {ew}, {EPI_WARP}, {base};")
-        b.ins(f"add.u32 {st_w}, {st_w}, {EPI};")
-        b.ins(f"shr.u32 {sub_row}, {lane}, 3;")
-        b.ins(f"and.b32 {sub_col}, {lane}, 7;")
-        b.ins(f"mad.lo.u32 {st_r}, {sub_row}, {EPI_ROW}, {st_w};")
-        b.ins(f"mad.lo.u32 {st_r}, {sub_col}, 16, {st_r};")
-        b.ins(f"shl.b32 {sub_col}, {sub_col}, 2;")
-        b.ins(f"mad.lo.u32 {st_w}, {lane}, {EPI_ROW}, {st_w};")
-
-    def stage_q(w, wait_free):
-        """Q of item w into TMEM (hi) and shared memory (lo), chunk by chunk.
-        The warp loads its 32 rows coalesced (lane l: dims 4l..4l+3 of a row,
-        512 bytes per instruction) while the previous item's QK^T still
-        runs.  Once that is complete (QF) it writes them into the Q lo region
-        (row r of each 32-dim box, 16-byte unit u at u ^ (r % 8): the K-major
-        128-byte-swizzle layout); then each thread reads its own row back,
-        32 dims at a time, scales it by scale * log2(e) (scores come out in
-        exp2 units), splits it into tf32 hi (TMEM) and lo = x - hi (in
-        place), and releases the chunk to the QK^T issuer (QR[c])."""
-        bh, qt, qi, pq, rowoff = row_of(w, etid)
-        wb, t1, w1 = b.regs("rd", 3)
-        b.ins(f"mul.wide.u32 {t1}, {etid}, {D * 4};")
-        b.ins(f"mul.wide.u32 {w1}, {wrow0}, {D * 4};")
-        b.ins(f"sub.s64 {wb}, {rowoff}, {t1};")
-        b.ins(f"add.s64 {wb}, {wb}, {w1};")
-        loff = b.reg("rd")
-        b.ins(f"mul.wide.u32 {loff}, {lane}, 16;")
-        b.ins(f"add.s64 {wb}, {wb}, {loff};")
-        b.ins(f"add.s64 {wb}, {wb}, {pQ};")
-        # the warp's first row within the sequence; rows at or past S (a
-        # partial last query tile) are zeros
-        qrow0 = b.reg("r")
-        b.ins(f"sub.u32 {qrow0}, {qi}, {etid};")
-        b.ins(f"add.u32 {qrow0}, {qrow0}, {wrow0};")
-        vals = []
-        for i in range(32):
-            v4 = b.regs("r", 4)
-            for e in range(4):
-                b.ins(f"mov.b32 {v4[e]}, 0;")
-            rr = b.reg("r")
-            b.ins(f"add.u32 {rr}, {qrow0}, {i};")
-            pr_ = b.reg("p")
-            b.ins(f"setp.lt.and.u32 {pr_}, {rr}, {S}, {pl_};")
-            b.ins(f"@{pr_} ld.global.nc.v4.b32 {{{', '.join(v4)}}}, [{wb}+{i * D * 4}];")
-            vals.append(v4)
-        if wait_free is not None:
-            tc.wait(bar_at("QF"), wait_free, END, ROLE_EPILOGUE, uniform=True,
-                    sleep_ns=EPI_SLEEP_NS)
-            b.ins("tcgen05.fence::after_thread_sync;")
-        for i in range(32):
-            ua = b.reg("r")
-            b.ins(f"xor.b32 {ua}, {lu}, {i % 8};")
-            b.ins(f"shl.b32 {ua}, {ua}, 4;")
-            b.ins(f"add.u32 {ua}, {ua}, {qst};")
-            b.ins(f"@{pl_} st.shared.v4.b32 [{ua}+{i * 128}], {{{', '.join(vals[i])}}};")
-        b.ins("bar.warp.sync 0xffffffff;")
-        for c in range(DC):
-            x, addrs = [], []
-            for u in range(8):
-                ua = b.reg("r")
-                b.ins(f"xor.b32 {ua}, {r8}, {u};")
-                b.ins(f"shl.b32 {ua}, {ua}, 4;")
-                b.ins(f"add.u32 {ua}, {ua}, {qrow};")
-                v4 = b.regs("f", 4)
-                b.ins(f"ld.shared.v4.f32 {{{', '.join(v4)}}}, [{ua}+{c * BQ * 128}];")
-                x += v4
-                addrs.append(ua)
-            hi = b.regs("r", 32)
-            lo = b.regs("r", 32)
-            for e in range(32):
-                # hi = x rounded to nearest tf32 (ties away) with two integer
-                # operations; lo = x - hi is exact.  A NaN or an infinity in
-                # Q still reaches S through lo.
-                b.ins(f"mul.f32 {x[e]}, {x[e]}, {f32_hex(qscale)};")
-                xb = b.reg("r")
-                b.ins(f"mov.b32 {xb}, {x[e]};")
-                b.ins(f"add.u32 {hi[e]}, {xb}, 4096;")
-                b.ins(f"and.b32 {hi[e]}, {hi[e]}, 0xFFFFE000;")
-                hf, lf = b.regs("f", 2)
-                b.ins(f"mov.b32 {hf}, {hi[e]};")
-                b.ins(f"sub.f32 {lf}, {x[e]}, {hf};")
-                b.ins(f"mov.b32 {lo[e]}, {lf};")
-            b.ins(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{ebase}+{C_QHI + 32 * c}], "
-                  f"{{{', '.join(hi)}}};")
-            for u in range(8):
-                b.ins(f"st.shared.v4.b32 [{addrs[u]}+{c * BQ * 128}], "
-                      f"{{{', '.join(lo[4 * u:4 * u + 4])}}};")
-            b.ins("tcgen05.wait::st.sync.aligned;")
-            b.ins("fence.proxy.async.shared::cta;")       # Q lo, for the tensor core
-            b.ins("tcgen05.fence::before_thread_sync;")
-            tc.arrive(bar_at("QR", c))
-
-    def epilogue(w):
-        """out = O / l for item w: after its last PV (OFIN) and its row sums
-        (LR), read O from TMEM, release it (OR), then store."""
-        bh, qt, qi, pq, rowoff = row_of(w, etid)
-        ib = b.reg("r")
-        b.ins(f"and.b32 {ib}, {it_e}, 1;")
-        hp = b.reg("r")
-        b.ins(f"shr.u32 {hp}, {it_e}, 1;")
-        b.ins(f"and.b32 {hp}, {hp}, 1;")
-        tc.wait(bar_at("LR", ib), hp, END, ROLE_EPILOGUE, uniform=True,
-                sleep_ns=EPI_SLEEP_NS)
-        tc.wait(bar_at("OFIN"), parity(it_e), END, ROLE_EPILOGUE, uniform=True,
-                sleep_ns=EPI_SLEEP_NS)
+        # the next item's Q: its buffers are free once this item's last
+        # QK^T is complete, which the last tile's S wait has seen
+        pn = b.reg("p")
+        nonext = b.label("NO_NEXT_Q")
+        b.ins(f"setp.ge.u32 {pn}, {kn}, {kend};")
+        b.ins(f"@{pn} bra.uni {nonext};")
+        stage_q(item_at(kn))
+        b.place(nonext)
+        # epilogue: wait for the item's last PV (one OFIN phase per item),
+        # out = O * (1 / l)
+        tc.wait(bar_at(OFIN), parity(it_x), END, ROLE_SOFTMAX, uniform=True)
         b.ins("tcgen05.fence::after_thread_sync;")
-        lb_ = b.reg("r")
-        b.ins(f"mad.lo.u32 {lb_}, {ib}, {BQ * 4}, {base};")
-        b.ins(f"mad.lo.u32 {lb_}, {etid}, 4, {lb_};")
-        lv = b.reg("f")
-        b.ins(f"ld.shared.f32 {lv}, [{lb_}+{LBUF}];")
         il = b.reg("f")
-        b.ins(f"rcp.rn.f32 {il}, {lv};")
-        ov = []
-        for c in range(DC):
-            o32 = b.regs("f", 32)
-            b.ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(o32)}}}, "
-                  f"[{ebase}+{C_O + 32 * c}];")
-            ov.append(o32)
-        b.ins("tcgen05.wait::ld.sync.aligned;")
-        b.ins("tcgen05.fence::before_thread_sync;")
-        tc.arrive(bar_at("OR"))
+        b.ins(f"rcp.rn.f32 {il}, {l_};")
         oaddr = b.reg("rd")
         b.ins(f"add.s64 {oaddr}, {rowoff}, {pO};")
         if gather:
             # rows of this warp's 32 queries in the [B*H*S, D] view
             rbase = b.reg("r")
             b.ins(f"mad.lo.u32 {rbase}, {qt}, {BQ}, {sub_row};")
-            b.ins(f"mad.lo.u32 {rbase}, {ew}, 32, {rbase};")
+            b.ins(f"mad.lo.u32 {rbase}, {warp}, 32, {rbase};")
             pbase = b.reg("r")
             b.ins(f"mad.lo.u32 {pbase}, {bh}, {S}, {grow0};")
             for c in range(DC):
+                ov = b.regs("f", 32)
+                b.ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, "
+                      f"[{lbase}+{C_O + 32 * c}];")
+                b.ins("tcgen05.wait::ld.sync.aligned;")
                 for g in range(8):
                     v4 = b.regs("f", 4)
                     for e in range(4):
-                        b.ins(f"mul.f32 {v4[e]}, {ov[c][4 * g + e]}, {il};")
+                        b.ins(f"mul.f32 {v4[e]}, {ov[4 * g + e]}, {il};")
                     b.ins(f"st.shared.v4.f32 [{st_w}+{16 * g}], {{{', '.join(v4)}}};")
                 b.ins("bar.warp.sync 0xffffffff;")
                 coff = b.reg("rd")
@@ -1199,12 +1227,12 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
                 b.ins(f"add.u32 {col}, {sub_col}, {32 * c};")
                 b.ins(f"mul.wide.u32 {coff}, {col}, 4;")
                 for i in range(8):
-                    wv = b.regs("f", 4)
-                    b.ins(f"ld.shared.v4.f32 {{{', '.join(wv)}}}, [{st_r}+{4 * i * EPI_ROW}];")
+                    w = b.regs("f", 4)
+                    b.ins(f"ld.shared.v4.f32 {{{', '.join(w)}}}, [{st_r}+{4 * i * EPI_ROW}];")
                     qr = b.reg("r")
                     b.ins(f"add.u32 {qr}, {rbase}, {4 * i};")
-                    prr = b.reg("p")
-                    b.ins(f"setp.lt.u32 {prr}, {qr}, {S};")
+                    pr = b.reg("p")
+                    b.ins(f"setp.lt.u32 {pr}, {qr}, {S};")
                     b.ins(f"add.u32 {qr}, {qr}, {pbase};")
                     ro = b.reg("rd")
                     b.ins(f"mul.wide.u32 {ro}, {qr}, {D * 4};")
@@ -1213,37 +1241,33 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
                         od, gd, pd = b.reg("rd"), b.reg("rd"), b.reg("p")
                         b.ins(f"ld.global.u64 {gd}, [emmy_gather_dst+{8 * d}];")
                         b.ins(f"add.s64 {od}, {ro}, {gd};")
-                        b.ins(f"setp.lt.and.u32 {pd}, {d}, {gn}, {prr};")
-                        b.ins(f"@{pd} st.global.v4.f32 [{od}], {{{', '.join(wv)}}};")
+                        b.ins(f"setp.lt.and.u32 {pd}, {d}, {gn}, {pr};")
+                        b.ins(f"@{pd} st.global.v4.f32 [{od}], {{{', '.join(w)}}};")
                 b.ins("bar.warp.sync 0xffffffff;")
-        else:
+        for c in range(0 if gather else DC):
+            ov = b.regs("f", 32)
+            b.ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, "
+                  f"[{lbase}+{C_O + 32 * c}];")
+            b.ins("tcgen05.wait::ld.sync.aligned;")
             # one thread writes its row: 32-byte stores (PTX ISA 8.8) fill
-            # whole sectors
-            for c in range(DC):
-                for g in range(32 // VW):
-                    vv = b.regs("f", VW)
-                    for e in range(VW):
-                        b.ins(f"mul.f32 {vv[e]}, {ov[c][VW * g + e]}, {il};")
-                    b.ins(f"@{pq} st.global.v{VW}.f32 [{oaddr}+{(32 * c + VW * g) * 4}], "
-                          f"{{{', '.join(vv)}}};")
-
-    def epi_item(w, kpos):
-        kn = b.reg("r")                   # the next item's position
-        b.ins(f"add.u32 {kn}, {kpos}, {kstep};")
-        pn = b.reg("p")
-        b.ins(f"setp.lt.u32 {pn}, {kn}, {kend};")
-        lb = skip_unless(pn, "NO_NEXT_Q")
-        stage_q(item_at(kn), parity(it_e))
-        b.place(lb)
-        epilogue(w)
-        b.ins(f"add.u32 {it_e}, {it_e}, 1;")
-
+            # whole sectors and halve the store instructions; the epilogue
+            # shares the memory pipe with the MMA threads' mbarrier polls as
+            # the next item starts
+            for g in range(32 // VW):
+                vv = b.regs("f", VW)
+                for e in range(VW):
+                    b.ins(f"mul.f32 {vv[e]}, {ov[VW * g + e]}, {il};")
+                b.ins(f"@{pq} st.global.v{VW}.f32 [{oaddr}+{(32 * c + VW * g) * 4}], "
+                      f"{{{', '.join(vv)}}};")
+        b.ins("tcgen05.fence::before_thread_sync;")
+        b.ins(f"add.u32 {it_x}, {it_x}, 1;")
     pfq = b.reg("p")
-    b.ins(f"setp.lt.u32 {pfq}, {kbeg}, {kend};")
-    lb = skip_unless(pfq, "NO_FIRST_Q")
-    stage_q(item_at(kbeg), None)          # the first item's Q
-    b.place(lb)
-    item_loop(epi_item, "EIT")
+    noq = b.label("NO_FIRST_Q")
+    b.ins(f"setp.ge.u32 {pfq}, {kbeg}, {kend};")
+    b.ins(f"@{pfq} bra.uni {noq};")
+    stage_q(item_at(kbeg))                # the first item's Q
+    b.place(noq)
+    item_loop(soft_item, "XIT")
 
     # ---- teardown -----------------------------------------------------------------
     b.place(END)
@@ -1252,9 +1276,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     # TMEM
     pd, pdl = b.reg("p"), b.label("PV_DRAINED")
     b.ins(f"setp.eq.u32 {pd}, {tid}, 224;")
+    b.ins(f"and.pred {pd}, {pd}, {lead};")
     b.ins(f"@!{pd} bra {pdl};")
-    tc.commit(bar_at("DRAIN2"))
-    tc.wait(bar_at("DRAIN2"), 0, pdl, ROLE_MMA, peer=False)
+    tc.commit(f"{bars}+{DRAIN2}")
+    tc.wait(f"{bars}+{DRAIN2}", 0, pdl, ROLE_MMA, peer=False)
     b.place(pdl)
     b.ins("bar.warp.sync 0xffffffff;")
     b.ins(f"bar.sync 0, {T};")
@@ -1266,8 +1291,23 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     dl = b.label("DRAIN_DONE")
     b.ins(f"setp.ne.u32 {pl}, {lane}, 0;")
     b.ins(f"@{pl} bra {dl};")
-    tc.commit(bar_at("DRAIN"))
-    tc.wait(bar_at("DRAIN"), 0, dl, ROLE_MMA)
+    if pair:
+        # the follower reports that it is done and then waits until the
+        # leader's MMAs (which write its TMEM and read its shared memory)
+        # have drained; the leader drains, waits for the follower, answers
+        fl = b.label("LEADER_FIN")
+        b.ins(f"@{lead} bra {fl};")
+        tc.arrive_cluster(remote(pbars, FIN))
+        tc.wait(f"{bars}+{FIN}", 0, dl, ROLE_MMA, peer=False)
+        b.ins(f"bra.uni {dl};")
+        b.place(fl)
+        tc.commit(f"{bars}+{DRAIN}")
+        tc.wait(f"{bars}+{DRAIN}", 0, dl, ROLE_MMA, peer=False)
+        tc.wait(f"{bars}+{FIN}", 0, dl, ROLE_MMA, peer=False)
+        tc.arrive_cluster(remote(pbars, FIN))
+    else:
+        tc.commit(f"{bars}+{DRAIN}")
+        tc.wait(f"{bars}+{DRAIN}", 0, dl, ROLE_MMA)
     b.place(dl)
     b.ins("bar.warp.sync 0xffffffff;")
     b.ins("tcgen05.fence::after_thread_sync;")
@@ -1279,9 +1319,9 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
 
     pairs = B * H * (S * (S + 1) // 2 if plan.causal else S * S)
     kv_tiles = 0                      # (128-query tile, 128-key tile) products issued
-    for qt in range(nqt):
-        keys = min(S, (qt + 1) * BQ) if plan.causal else S
-        kv_tiles += -(-keys // BKV)
+    for qu in range(nqu):
+        keys = min(S, (qu + 1) * BQ * CG) if plan.causal else S
+        kv_tiles += CG * -(-keys // BKV)
     kv_tiles *= B * H
     # tensor work actually issued: S (3 products) and PV (1 product) per key tile
     issued = kv_tiles * (3 * 2 * BQ * BKV * D + 2 * BQ * D * BKV)
@@ -1291,10 +1331,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
                                "box": [32, BOX_KEYS, 1], "swizzle": sw}
     sidecar = {
         "category": "attention",
-        "grid": [min(items, 148), 1, 1],
+        "grid": [CG * min(items, 148 // CG), 1, 1],
         "block": [T, 1, 1],
         "shared_bytes": SMEM,
-        "cluster": [1, 1, 1],
+        "cluster": [CG, 1, 1],
         "scratch": [{"name": "k_lo", "bytes": kbytes},
                     {"name": "v_r", "bytes": kbytes}],
         "prelaunch": [split_launch(split_entry, [plan.k, plan.v, "@k_lo", "@v_r"],
@@ -1304,9 +1344,8 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
                        tmap("tmap_V", "@v_r", "128B_atom32B")],
         "algorithmic_flops": 4 * pairs * D,
         "tensor_flops_issued": issued,
-        "tile": [BQ, BKV, D],
-        "cta_group": 1,
-        "launch_registers": REG_LAUNCH,
+        "tile": [BQ * CG, BKV, D],
+        "cta_group": CG,
         "status_word": "emmy_status",
     }
     if gather:

@@ -171,17 +171,14 @@ class TC:
         self.b.ins(f"mbarrier.arrive.expect_tx.shared::cta.b64 {st}, [{bar}], {nbytes};")
 
     def wait(self, bar, parity, fail_label, role: int, uniform: bool = False,
-             peer: bool = True, sleep_ns: int = 0):
+             peer: bool = True):
         """Bounded wait for the phase of parity ``parity`` (register or
         immediate) of ``bar``; on timeout or abort branch to
         ``fail_label``.  ``uniform``: every lane of the warp waits and all
         decisions are warp votes, so the warp leaves converged (needed
         before ``.sync.aligned`` instructions).  ``peer``: a timeout also
         raises the pair peer's abort flag (off in teardown waits, when the
-        peer may already have exited).  ``sleep_ns``: after a poll that
-        finds the phase incomplete, sleep about that long before the next
-        (for warps that wait long, so that their polls leave the issue slots
-        of their SM sub-partition to the warps that work)."""
+        peer may already have exited)."""
         b = self.b
         top, done = b.label("WAIT"), b.label("WAIT_OK")
         p, pf, pv = b.regs("p", 3)
@@ -199,8 +196,6 @@ class TC:
         b.ins(f"mov.u64 {t0}, %globaltimer;")
         b.ins(f"mov.u32 {n}, 0;")
         b.place(top)
-        if sleep_ns:
-            b.ins(f"nanosleep.u32 {int(sleep_ns)};")
         b.ins(f"mbarrier.try_wait.parity.shared::cta.b64 {p}, [{bar}], {parity};")
         if uniform:
             b.ins(f"vote.sync.all.pred {pv}, {p}, 0xffffffff;")

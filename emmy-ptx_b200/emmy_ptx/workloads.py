@@ -657,11 +657,9 @@ def matmul_fp8(m=8192, n=8192, k=8192, fmt="e4m3") -> Problem:
 
 # -- config 5: attention -----------------------------------------------------
 def attention(batch=8, heads=32, seq=4096, head_dim=128, causal=True, scale=None,
-              block=384) -> Problem:
+              block=256) -> Problem:
     """Causal self-attention, online softmax, one warp per query row; each
-    lane owns head_dim/32 dimensions of q and of the output accumulator.
-    Blocks of 12 warps (12 query rows per block in this per-row form; the
-    sm_100a kernel's 12 warps: softmax, producers and MMA, epilogue)."""
+    lane owns head_dim/32 dimensions of q and of the output accumulator."""
     assert head_dim % 32 == 0 and head_dim // 32 in (1, 2, 4)
     dpl = head_dim // 32
     scale = 1.0 / math.sqrt(head_dim) if scale is None else float(scale)

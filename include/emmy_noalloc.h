@@ -52,9 +52,7 @@ extern "C" {
  * 2 * align256(heads_total*seq*head_dim*4) exceeds ERT_NOALLOC_SCRATCH_BYTES,
  * and ERT_E_ARGUMENT, without launching, when heads_total/seq/head_dim is not
  * the shape `module` was compiled for (recorded in the module as the global
- * emmy_attn_shape_<heads_total>x<seq>x<head_dim>), or when the kernel was
- * loaded with a register count per thread other than the one its register
- * split assumes (recorded as emmy_launch_regs_<n>); other codes as in
+ * emmy_attn_shape_<heads_total>x<seq>x<head_dim>); other codes as in
  * emmy_rt.h.  Calls share the scratch and rewrite the module's tensor-map
  * globals: calls that overlap in time race, so keep them on one stream, and
  * do not also launch the same module through emmy_ptx.runtime.Kernel (it

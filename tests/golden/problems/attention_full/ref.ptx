@@ -28,7 +28,7 @@
         and.b32 %r2, %r1, 31;
         shr.u32 %r3, %r1, 5;
         mov.u32 %r4, %ctaid.x;
-        mad.lo.u32 %r5, %r4, 384, %r1;
+        mad.lo.u32 %r5, %r4, 256, %r1;
         setp.ge.u32 %p1, %r5, 33554432;
         @%p1 bra TILE_END_1;
         div.s32 %r6, %r5, 4194304;

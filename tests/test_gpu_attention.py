@@ -79,23 +79,31 @@ def test_non_finite_values_propagate_like_the_reference(cuda):
 
 
 @pytest.mark.gpu
-def test_launch_register_count_is_checked_before_any_launch(cuda):
-    """The kernel's warpgroups re-divide their registers (setmaxnreg); its
-    sidecar states the registers per thread the split assumes at launch.  A
-    loaded kernel with any other count is refused before it is launched."""
+@pytest.mark.parametrize("kw", [dict(batch=1, heads=3, seq=640, head_dim=128, causal=True),
+                                dict(batch=2, heads=1, seq=300, head_dim=64, causal=True),
+                                dict(batch=1, heads=2, seq=384, head_dim=128, causal=False)],
+                         ids=["640c", "300x64c", "384n"])
+def test_cta_pair_kernel_matches_float64_reference(cuda, kw):
+    """The CTA-pair variant (tcgen05 cta_group::2, 256 query rows per pair,
+    half of every K and V chunk per CTA), forced on: a partial last pair,
+    head_dim 64 and 128, causal (the lower tile's last key tile fully
+    masked) and not."""
     from emmy_ptx import workloads
     from emmy_ptx.compiler import Compiler
-    from emmy_ptx.runtime import EmmyRuntimeError, Kernel
-    p = workloads.attention(batch=1, heads=2, seq=256, head_dim=64)
+    from emmy_ptx.runtime import Kernel
+    from emmy_ptx.sm100 import attention
+    p = workloads.attention(**kw)
+    inputs = p.make_inputs()
     with tempfile.TemporaryDirectory() as td:
-        comp = Compiler(p.write(td), target="sm_100a", ptx_version="8.8")
-        ptx, side = comp.compile(), comp.sidecar()
-    geom = {"grid": comp.kmeta["grid"], "block": comp.kmeta["block"]}
-    k = Kernel(ptx, comp.entry, Kernel._arg_specs(comp), geom, side)
-    assert k.module.attrs(comp.entry)["num_regs"] == side["launch_registers"]
-    bad = dict(side, launch_registers=side["launch_registers"] - 8)
-    with pytest.raises(EmmyRuntimeError, match="register split"):
-        Kernel(ptx, comp.entry, Kernel._arg_specs(comp), geom, bad)
+        comp = Compiler(p.write(td), target="sm_100a", ptx_version="8.7")
+        ptx, side = attention.emit(comp, attention.match(comp), pair=True)
+        assert side["cluster"] == [2, 1, 1] and side["cta_group"] == 2
+        kern = Kernel(ptx, comp.entry, Kernel._arg_specs(comp),
+                      {"grid": comp.kmeta["grid"], "block": comp.kmeta["block"]}, side)
+        got = run_on_gpu(kern, p, inputs, cuda)
+    want = _reference(inputs, p.params["scale"], kw["causal"])
+    ok, msg = check_close("attention", "out", got["out"], want, inputs, causal=kw["causal"])
+    assert ok, msg
 
 
 @pytest.mark.gpu

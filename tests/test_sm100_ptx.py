@@ -184,28 +184,3 @@ def test_row_gather_variant_stores_to_every_destination(tmp_path, name, kw):
     report = _build.ptxas_check(ptx)
     assert "0 bytes spill stores" in report, report
 
-
-def test_attention_register_split_fits_the_launch(tmp_path):
-    """The attention kernel's warpgroups re-divide their registers with
-    setmaxnreg: the producer/MMA warpgroup gives some back before the
-    softmax and epilogue warpgroups take more.  setmaxnreg.inc waits until
-    the block's registers allow it, so the three shares (128 threads each)
-    must add up to no more than the launch's 384 x .maxnreg; ptxas assembles
-    it at exactly that count without spills, and the module names the count
-    (checked by launchers before the first launch)."""
-    import re
-    from emmy_ptx import workloads
-    from emmy_ptx.sm100 import attention
-    p = workloads.attention(batch=1, heads=4, seq=640, head_dim=128)
-    comp = Compiler(p.write(tmp_path), target="sm_100a", ptx_version="8.8")
-    ptx, side = attention.emit(comp, attention.match(comp))
-    launch = int(re.search(r"\.maxnreg (\d+)", ptx).group(1))
-    incs = [int(x) for x in re.findall(r"setmaxnreg\.inc\.sync\.aligned\.u32 (\d+);", ptx)]
-    decs = [int(x) for x in re.findall(r"setmaxnreg\.dec\.sync\.aligned\.u32 (\d+);", ptx)]
-    assert len(incs) == 2 and len(decs) == 1
-    assert 128 * (sum(incs) + sum(decs)) <= attention.THREADS * launch
-    assert all(x % 8 == 0 and 24 <= x <= 256 for x in incs + decs + [launch])
-    assert side["launch_registers"] == launch and side["block"] == [attention.THREADS, 1, 1]
-    assert f"emmy_launch_regs_{launch}" in ptx
-    report = _build.ptxas_check(ptx)
-    assert f"Used {launch} registers" in report and "0 bytes spill stores" in report, report
