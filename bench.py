@@ -226,24 +226,24 @@ def time_kernel(bound, reps, warmup, stream):
 # ----------------------------------------------------------------------------
 # end to end through the host-buffer C-ABI path
 # ----------------------------------------------------------------------------
-def link_gbs(device, nbytes=256 << 20, reps=3):
-    """Host <-> device copy bandwidth with both directions in flight at once
+def link_probe(device, h2d_bytes, d2h_bytes, barrier, max_over_ranks, reps=3):
+    """The ceiling of the end-to-end step: the same volume moved the same way
+    with no kernels -- every rank copies its step's inputs in and outputs out
     (pinned host buffers, one stream per direction, one cudaMemcpyAsync per
-    copy): the ceiling of the end-to-end step, which moves its inputs in and
-    its outputs out over the same link.  ``nbytes`` each way (the step's
-    own volume, so the ceiling is taken over as long a transfer); best of
-    ``reps`` after a warm-up."""
+    direction, both in flight at once), all ranks starting together after a
+    barrier, timed with CUDA events, max over ranks; best of ``reps`` after
+    a warm-up.  Returns (ms, this rank's own ms)."""
     import torch
-    n = nbytes // 4
-    h_in = torch.empty(n, dtype=torch.float32).pin_memory()
-    h_out = torch.empty(n, dtype=torch.float32).pin_memory()
-    d_in = torch.empty(n, device=device)
-    d_out = torch.zeros(n, device=device)
+    h_in = torch.empty(h2d_bytes // 4, dtype=torch.float32).pin_memory()
+    h_out = torch.empty(d2h_bytes // 4, dtype=torch.float32).pin_memory()
+    d_in = torch.empty(h2d_bytes // 4, device=device)
+    d_out = torch.zeros(d2h_bytes // 4, device=device)
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     cur = torch.cuda.current_stream(device)
-    best = None
+    best = mine = None
     for i in range(reps + 1):
         torch.cuda.synchronize(device)
+        barrier()
         a, e = _events(2)
         a.record(cur)
         s_in.wait_stream(cur)
@@ -256,11 +256,13 @@ def link_gbs(device, nbytes=256 << 20, reps=3):
         cur.wait_stream(s_out)
         e.record(cur)
         torch.cuda.synchronize(device)
+        t = a.elapsed_time(e)
+        tmax = max_over_ranks(t)
         if i:
-            t = a.elapsed_time(e)
-            best = t if best is None else min(best, t)
+            if best is None or tmax < best:
+                best, mine = tmax, t
     del h_in, h_out, d_in, d_out
-    return 2 * nbytes / best / 1e6
+    return best, mine
 
 
 def e2e_measure(names, workdir, steps, warmup, seed_offset, chunks=32, slots=3, rows_div=1):
@@ -666,21 +668,21 @@ def run_b200(args):
     torch.cuda.empty_cache()
 
     # end to end through the host-buffer API: each rank moves its own rows
-    chunks = max(4, 32 // world)
+    chunks = 32
     barrier()
     e2e = e2e_measure(HEADLINE, workdir, max(3, args.steps // 4), 2, rank,
                       chunks=chunks, rows_div=world)
     et = max_over_ranks(e2e["ms_per_step"])
     e2e_value = world * e2e["bytes"] / et / 1e6
-    # every rank's link, both ways at once, all ranks copying together
-    barrier()
-    mine = link_gbs(device, nbytes=max(e2e["h2d"], e2e["d2h"]) // 4 * 4)
-    links = [mine]
+    # the same copies with no kernels, all ranks at once: the step's ceiling
+    link_ms, link_mine = link_probe(device, e2e["h2d"] // 4 * 4, e2e["d2h"] // 4 * 4,
+                                    barrier, max_over_ranks)
+    link_total = world * (e2e["h2d"] + e2e["d2h"]) / link_ms / 1e6
+    links = [round((e2e["h2d"] + e2e["d2h"]) / link_mine / 1e6, 1)]
     if world > 1:
         allv = [None] * world
-        dist.all_gather_object(allv, mine)
+        dist.all_gather_object(allv, links[0])
         links = allv
-    link_total = sum(links)
     pcie_total = world * (e2e["h2d"] + e2e["d2h"]) / et / 1e6
 
     if world > 1:
@@ -713,7 +715,10 @@ def run_b200(args):
                 "h2d_bytes_per_step": e2e["h2d"] * world, "d2h_bytes_per_step": e2e["d2h"] * world,
                 "ms_per_step": round(et, 3),
                 "link_both_ways_gbs": round(link_total, 1),
-                "link_per_rank_gbs": [round(x, 1) for x in links],
+                "link_ms_per_step": round(link_ms, 3),
+                "link_per_rank_gbs": links,
+                "link": "the step's copies alone (no kernels), both directions at once, "
+                        "all ranks together, max over ranks",
                 "frac_of_link": round(pcie_total / link_total, 3),
                 "path": f"emmy_ptx.pipeline.ChunkedHostRunner: pinned host -> ert_memcpy_htod "
                         f"-> launch -> ert_memcpy_dtoh, {e2e['chunks']} row blocks per rank "

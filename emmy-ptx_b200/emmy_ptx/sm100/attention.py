@@ -79,6 +79,9 @@ PAIR_VS = 4        #            V ring slots of half chunks
 PAIR = False
 LOG2E = 1.4426950408889634
 ROLE_SOFTMAX, ROLE_PRODUCER, ROLE_MMA = 5, 6, 7
+# arrivals of the softmax warps on the barriers the MMA issuers wait on (P
+# ready, Q ready): 4 = one per warp, 128 = one per thread
+ARRIVALS = 4
 
 
 @dataclass
@@ -386,10 +389,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     for s in range(NVS):
         for off in (VF, VE):
             tc.init(f"{bars}+{off + 8 * s}", 1)
-    tc.init(f"{bars}+{QR}", 128 * CG)         # every softmax thread of the pair
+    tc.init(f"{bars}+{QR}", ARRIVALS * CG)    # the softmax warps of the pair
     for k in range(2):
         tc.init(f"{bars}+{SF + 8 * k}", 1)
-        tc.init(f"{bars}+{PF + 8 * k}", 128 * CG)
+        tc.init(f"{bars}+{PF + 8 * k}", ARRIVALS * CG)
     tc.init(f"{bars}+{OF}", 1)
     tc.init(f"{bars}+{OFIN}", 1)
     tc.init(f"{bars}+{DRAIN}", 1)
@@ -923,11 +926,23 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
 
     def to_leader(off, s=None):
         """Arrive on barrier off(+8s) of the MMA-issuing CTA: this CTA's,
-        or the pair leader's."""
+        or the pair leader's.  With one arrival per warp, the warp first
+        synchronises (its lanes' TMEM and shared-memory writes, each already
+        complete and fenced, are then ordered before lane 0's arrival), and
+        lane 0 arrives for all 32."""
+        if ARRIVALS == 4:
+            b.ins("bar.warp.sync 0xffffffff;")
+            pa = b.reg("p")
+            b.ins(f"setp.eq.u32 {pa}, {lane}, 0;")
+            sk = b.label("ARRIVED")
+            b.ins(f"@!{pa} bra {sk};")
         if pair:
             tc.arrive_cluster(remote(lbars, off, s))
         else:
             tc.arrive(bar_at(off, s))
+        if ARRIVALS == 4:
+            b.place(sk)
+            b.ins("bar.warp.sync 0xffffffff;")
 
     def row_of(w):
         """Item w: (bh, query unit, this CTA's query tile, this thread's
