@@ -82,7 +82,7 @@ class _Slot:
 
 
 class ChunkedHostRunner:
-    def __init__(self, name: str, chunks: int = 32, slots: int = 3, workdir=None,
+    def __init__(self, name: str, chunks: int = 16, slots: int = 3, workdir=None,
                  streams: PipelineStreams | None = None, **kw):
         if dist.PARTITION[name] != "rows":
             raise ValueError(f"{name} is not partitioned by rows")
