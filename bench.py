@@ -172,39 +172,6 @@ def _events(n):
     return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
 
 
-def time_steps(bounds, steps, warmup, stream, barrier):
-    """W warm-up steps, then K timed steps bracketed by barrier + sync.
-    Returns (step ms, per-kernel average ms)."""
-    import torch
-    with torch.cuda.stream(stream):
-        for _ in range(warmup):
-            for b in bounds:
-                b.launch()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    marks = _events(steps * len(bounds) + 1)
-    with torch.cuda.stream(stream):
-        marks[0].record(stream)
-        i = 1
-        for _ in range(steps):
-            for b in bounds:
-                b.launch()
-                marks[i].record(stream)
-                i += 1
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    total = marks[0].elapsed_time(marks[-1])
-    per = [0.0] * len(bounds)
-    i = 1
-    for _ in range(steps):
-        for j in range(len(bounds)):
-            per[j] += marks[i - 1].elapsed_time(marks[i])
-            i += 1
-    return total / steps, [x / steps for x in per]
-
-
 def time_kernel(bound, reps, warmup, stream):
     """Average device time of back-to-back launches (inputs > L2 or
     compute-bound, as stated per category)."""
