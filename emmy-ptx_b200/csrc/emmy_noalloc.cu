@@ -183,11 +183,12 @@ extern "C" int ert_attention_noalloc(uint64_t module, uint64_t attention_fn, uin
                            kSwizzle128Atom32, stream, err, err_len);
     if (rc) return rc;
 
-    // pre-pass: K -> lo and V -> tf32-rounded V, grid-stride over 16-byte
-    // vectors
+    // pre-pass: K -> lo and V -> tf32-rounded V; a grid-stride loop, so any
+    // grid covers it: 16 blocks of 256 threads per SM, as the regular launch
+    // uses (fewer when the problem is smaller)
     const uint64_t nvec = kbytes / 16;
     uint64_t blocks = (nvec + 255) / 256;
-    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks > 148 * 16) blocks = 148 * 16;
     ert_geom pg = {{unsigned(blocks), 1, 1}, {256, 1, 1}, {1, 1, 1}, 0};
     void *pargs[4] = {&k, &v, &lo, &vr};
     rc = ert_launch(ksplit_fn, &pg, pargs, stream);

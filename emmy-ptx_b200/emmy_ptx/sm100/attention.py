@@ -164,8 +164,13 @@ def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: 
     hi = K with the low 13 bits cleared) and this entry writes only
     ``lo = K - hi`` (exact).  V is rounded to the nearest tf32 value
     (``cvt.rna``: ties away from zero; NaN and infinity kept), so that the
-    tensor core reads V unbiased.  Grid-stride over 16-byte vectors;
-    ``n_elems`` a multiple of 4; returned without the module header."""
+    tensor core reads V unbiased.  Grid-stride over vectors of 8 floats
+    (32-byte accesses, PTX ISA 8.8) or 4 below 8.8; ``n_elems`` a multiple
+    of the vector; returned without the module header.  With 32-byte
+    vectors and 16 blocks per SM the full-size pass (2 GB) measured 0.332
+    ms against 0.368 with 16-byte vectors and 8 blocks per SM."""
+    vw = 8 if wide_vectors(version) else 4
+    assert n_elems % vw == 0
     b = KernelBuilder(entry, target, version)
     b.directive(f".maxntid {block}, 1, 1")
     names = ("k", "v", "k_lo", "v_r")
@@ -186,20 +191,20 @@ def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: 
     top, done = b.label("PRE"), b.label("PRE_END")
     p = b.reg("p")
     b.place(top)
-    b.ins(f"setp.ge.u32 {p}, {g}, {n_elems // 4};")
+    b.ins(f"setp.ge.u32 {p}, {g}, {n_elems // vw};")
     b.ins(f"@{p} bra {done};")
     off = b.reg("rd")
-    b.ins(f"mul.wide.u32 {off}, {g}, 16;")
+    b.ins(f"mul.wide.u32 {off}, {g}, {vw * 4};")
     a = {nm: b.reg("rd") for nm in names}
     for nm, base_ in zip(names, ptrs):
         b.ins(f"add.s64 {a[nm]}, {base_}, {off};")
-    x = b.regs("f", 4)
-    y = b.regs("f", 4)
-    b.ins(f"ld.global.nc.L1::no_allocate.v4.f32 {{{', '.join(x)}}}, [{a['k']}];")
-    b.ins(f"ld.global.nc.L1::no_allocate.v4.f32 {{{', '.join(y)}}}, [{a['v']}];")
-    vr = b.regs("r", 4)
-    lo = b.regs("f", 4)
-    for e in range(4):
+    x = b.regs("f", vw)
+    y = b.regs("f", vw)
+    b.ins(f"ld.global.nc.L1::no_allocate.v{vw}.f32 {{{', '.join(x)}}}, [{a['k']}];")
+    b.ins(f"ld.global.nc.L1::no_allocate.v{vw}.f32 {{{', '.join(y)}}}, [{a['v']}];")
+    vr = b.regs("r", vw)
+    lo = b.regs("f", vw)
+    for e in range(vw):
         hb = b.reg("r")
         b.ins(f"mov.b32 {hb}, {x[e]};")
         b.ins(f"and.b32 {hb}, {hb}, 0xFFFFE000;")
@@ -207,8 +212,8 @@ def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: 
         b.ins(f"mov.b32 {hf}, {hb};")
         b.ins(f"sub.f32 {lo[e]}, {x[e]}, {hf};")
         b.ins(f"cvt.rna.tf32.f32 {vr[e]}, {y[e]};")
-    b.ins(f"st.global.v4.f32 [{a['k_lo']}], {{{', '.join(lo)}}};")
-    b.ins(f"st.global.v4.b32 [{a['v_r']}], {{{', '.join(vr)}}};")
+    b.ins(f"st.global.v{vw}.f32 [{a['k_lo']}], {{{', '.join(lo)}}};")
+    b.ins(f"st.global.v{vw}.b32 [{a['v_r']}], {{{', '.join(vr)}}};")
     b.ins(f"add.u32 {g}, {g}, {stride};")
     b.ins(f"bra.uni {top};")
     b.place(done)
@@ -1353,7 +1358,8 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         "scratch": [{"name": "k_lo", "bytes": kbytes},
                     {"name": "v_r", "bytes": kbytes}],
         "prelaunch": [split_launch(split_entry, [plan.k, plan.v, "@k_lo", "@v_r"],
-                                   B * H * S * D)],
+                                   B * H * S * D, max_blocks=148 * 16,
+                                   vec=8 if wide_vectors(comp.ptx_version) else 4)],
         "tensormaps": [tmap("tmap_Khi", plan.k, "128B"),     # K itself: hi = K, low bits dropped
                        tmap("tmap_Klo", "@k_lo", "128B"),
                        tmap("tmap_V", "@v_r", "128B_atom32B")],

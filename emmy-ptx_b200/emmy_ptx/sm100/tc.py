@@ -121,11 +121,13 @@ def emit_tf32_split(target: str, version: str, entry: str, n_elems: int,
     return b.render(header=False)
 
 
-def split_launch(entry: str, args: list, n_elems: int, block: int = 256) -> dict:
-    """The sidecar ``prelaunch`` record for an ``emit_tf32_split`` entry."""
-    nvec = n_elems // 4
+def split_launch(entry: str, args: list, n_elems: int, block: int = 256,
+                 max_blocks: int = 148 * 8, vec: int = 4) -> dict:
+    """The sidecar ``prelaunch`` record for a grid-stride split entry over
+    ``vec``-element vectors, at most ``max_blocks`` blocks."""
+    nvec = n_elems // vec
     return {"entry": entry, "args": list(args),
-            "grid": [max(1, min(-(-nvec // block), 148 * 8)), 1, 1], "block": [block, 1, 1]}
+            "grid": [max(1, min(-(-nvec // block), max_blocks)), 1, 1], "block": [block, 1, 1]}
 
 
 def idesc_f8(m: int, n: int, a_mn_major: bool, b_mn_major: bool, ab: str = "e4m3") -> int:
