@@ -51,6 +51,7 @@ struct Driver {
     ERT_FN(cuTensorMapEncodeTiled)
     ERT_FN(cuMemcpyHtoDAsync)
     ERT_FN(cuMemcpyDtoHAsync)
+    ERT_FN(cuMemcpyDtoDAsync)
     ERT_FN(cuMemsetD8Async)
     ERT_FN(cuStreamSynchronize)
     ERT_FN(cuStreamCreate)
@@ -99,6 +100,7 @@ struct Driver {
         ERT_LOAD(cuTensorMapEncodeTiled)
         ERT_LOAD(cuMemcpyHtoDAsync)
         ERT_LOAD(cuMemcpyDtoHAsync)
+        ERT_LOAD(cuMemcpyDtoDAsync)
         ERT_LOAD(cuMemsetD8Async)
         ERT_LOAD(cuStreamSynchronize)
         ERT_LOAD(cuStreamCreate)
@@ -371,6 +373,17 @@ int ert_memcpy_dtoh(void *dst, uint64_t src, size_t bytes, uint64_t stream) {
     return check(drv().cuMemcpyDtoHAsync(dst, static_cast<CUdeviceptr>(src), bytes,
                                          reinterpret_cast<CUstream>(stream)),
                  "cuMemcpyDtoHAsync");
+}
+
+int ert_memcpy_dtod(uint64_t dst, uint64_t src, size_t bytes, uint64_t stream) {
+    ERT_NEED_DRIVER();
+    int rc;
+    if ((rc = need_ctx())) return rc;
+    if (!bytes) return 0;
+    return check(drv().cuMemcpyDtoDAsync(static_cast<CUdeviceptr>(dst),
+                                         static_cast<CUdeviceptr>(src), bytes,
+                                         reinterpret_cast<CUstream>(stream)),
+                 "cuMemcpyDtoDAsync");
 }
 
 int ert_memset_d8(uint64_t dst, unsigned char value, size_t bytes, uint64_t stream) {

@@ -336,6 +336,104 @@ class FusedGather:
         self.out.close()
 
 
+class CopyGather:
+    """Rank ``rank``'s shard of a row problem ("rmsnorm", "softmax", ...)
+    whose output all-gather runs on the copy engines: the shard's kernel
+    writes its rows straight into this rank's full output (``out.local``, at
+    the shard's row offset), then one device-to-device copy per peer
+    (``ert_memcpy_dtod`` into the peer's full output, mapped with CUDA IPC)
+    moves them over NVLink, one stream per peer so the copies run on several
+    engines at once.  With ``chunks`` > 1 the shard runs as that many row
+    blocks, and a block's copies overlap the next block's kernel.  After
+    ``launch()`` and ``wait()`` on every rank, ``out.local`` holds the full
+    output everywhere."""
+
+    def __init__(self, name: str, rank: int, world: int, workdir, chunks: int = 1,
+                 group=None, **kw):
+        from .runtime import Event, Kernel, Stream
+        if PARTITION[name] != "rows":
+            raise ValueError(f"{name} is not partitioned by rows")
+        self.name, self.rank, self.world, self.group = name, rank, world, group
+        self.part, self.full = shard_problem(name, rank, world, **kw)
+        sub, _ = shard_problem(name, rank * chunks, world * chunks, **kw)
+        self.chunks = chunks
+        self.kernel = Kernel.from_ir(sub.write(os.path.join(workdir, f"copyg_{name}_{rank}")))
+        out = self.part.outputs[0]
+        self.out_name = out
+        self.row_bytes = self.full["cols"] * 4
+        self.rows = self.part.tensor(out)["shape"][0]          # this rank's rows
+        self.sub_rows = sub.tensor(out)["shape"][0]
+        self.row0 = rank * self.rows
+        self.out = PeerBuffer(self.full["rows"] * self.row_bytes, group)
+        self.copy_streams = [Stream() for _ in range(world)]
+        self.k_done = [Event() for _ in range(chunks)]
+        self.c_done = [Event() for _ in range(world)]
+        self._launches = None
+
+    def bind(self, buffers: dict, stream=None):
+        """``buffers``: the shard's inputs (this rank's rows; their row-split
+        tensors are cut into the chunks here).  The output argument is this
+        rank's rows of ``out.local``."""
+        from .runtime import _stream_handle
+        self.stream = _stream_handle(stream)
+        self._launches = []
+        for c in range(self.chunks):
+            bufs = {}
+            for t in self.part.inputs:
+                ten = buffers[t]
+                split = self.part.tensor(t)["shape"][0] == self.rows and \
+                    len(self.part.tensor(t)["shape"]) > 1
+                ptr = ten.data_ptr() if hasattr(ten, "data_ptr") else int(ten)
+                if split:
+                    ptr += c * self.sub_rows * self.part.tensor(t)["shape"][1] * \
+                        ten.element_size()
+                bufs[t] = ptr
+            bufs[self.out_name] = self.out.local.ptr + (self.row0 + c * self.sub_rows) * \
+                self.row_bytes
+            self._launches.append(self.kernel.bind(bufs, stream=self.stream))
+        return self
+
+    def launch(self):
+        from .runtime import check, lib
+        L = lib()
+        nbytes = self.sub_rows * self.row_bytes
+        for c, launch in enumerate(self._launches):
+            launch()
+            self.k_done[c].record(self.stream)
+            off = (self.row0 + c * self.sub_rows) * self.row_bytes
+            for i in range(1, self.world):
+                d = (self.rank + i) % self.world
+                cs = self.copy_streams[d]
+                cs.wait(self.k_done[c])
+                check(L.ert_memcpy_dtod(self.out.ptrs[d] + off, self.out.local.ptr + off,
+                                        nbytes, cs.handle), "ert_memcpy_dtod")
+        # the launching stream waits for every copy
+        for i in range(1, self.world):
+            d = (self.rank + i) % self.world
+            self.c_done[d].record(self.copy_streams[d])
+            check(L.ert_stream_wait_event(self.stream, self.c_done[d].handle),
+                  "ert_stream_wait_event")
+
+    def wait(self):
+        """Stream-ordered completion barrier: a one-element all-reduce that
+        finishes only after every rank's copies into this rank have."""
+        import torch
+        import torch.distributed as dist
+        if not hasattr(self, "_flag"):
+            self._flag = torch.zeros(1, dtype=torch.int32,
+                                     device=torch.device("cuda", torch.cuda.current_device()))
+        dist.all_reduce(self._flag, group=self.group)
+
+    def close(self):
+        for s in self.copy_streams:
+            s.synchronize()
+        self.out.close()
+        for s in self.copy_streams:
+            s.destroy()
+        for e in self.k_done + self.c_done:
+            e.destroy()
+
+
 class FusedGatherMatmul(FusedGather):
     """``FusedGather("matmul", ...)``."""
 

@@ -71,6 +71,8 @@ _SIGS = {
                         ctypes.c_int),
     "ert_memcpy_dtoh": ([ctypes.c_void_p, ctypes.c_uint64, ctypes.c_size_t, ctypes.c_uint64],
                         ctypes.c_int),
+    "ert_memcpy_dtod": ([ctypes.c_uint64, ctypes.c_uint64, ctypes.c_size_t, ctypes.c_uint64],
+                        ctypes.c_int),
     "ert_memset_d8": ([ctypes.c_uint64, ctypes.c_ubyte, ctypes.c_size_t, ctypes.c_uint64],
                       ctypes.c_int),
     "ert_stream_sync": ([ctypes.c_uint64], ctypes.c_int),

@@ -88,6 +88,9 @@ int ert_tensormap_encode(void *out, int dtype, int rank, uint64_t global_addr,
 /* Stream-ordered copies and fill (asynchronous on `stream`). */
 int ert_memcpy_htod(uint64_t dst, const void *src, size_t bytes, uint64_t stream);
 int ert_memcpy_dtoh(void *dst, uint64_t src, size_t bytes, uint64_t stream);
+/* Device to device, one copy per call; with `dst` a peer's buffer mapped by
+ * ert_ipc_open the copy engines move it over NVLink. */
+int ert_memcpy_dtod(uint64_t dst, uint64_t src, size_t bytes, uint64_t stream);
 int ert_memset_d8(uint64_t dst, unsigned char value, size_t bytes, uint64_t stream);
 int ert_stream_sync(uint64_t stream);
 

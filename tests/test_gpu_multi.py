@@ -23,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out_dir, name):
+def _worker(rank, world, port, out_dir, name, mode="fused"):
     import sys
     from datetime import timedelta
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -48,7 +48,10 @@ def _worker(rank, world, port, out_dir, name):
         inputs = full.make_inputs()
         shard = edist.shard_inputs(name, inputs, rank, world)
         stream = torch.cuda.Stream(device)
-        fused = edist.FusedGather(name, rank, world, out_dir, **kw)
+        if mode == "copy":
+            fused = edist.CopyGather(name, rank, world, out_dir, chunks=2, **kw)
+        else:
+            fused = edist.FusedGather(name, rank, world, out_dir, **kw)
         dev = {n: torch.from_numpy(v).to(device) for n, v in shard.items()}
         out = fused.part.outputs[0]
         dev[out] = torch.empty(fused.part.tensor(out)["shape"], dtype=torch.float32,
@@ -73,7 +76,8 @@ def _worker(rank, world, port, out_dir, name):
         assert fused.kernel.status() == 0
         dist.barrier()
         fused.close()
-        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), first=results[0], second=results[1])
+        np.savez(os.path.join(out_dir, f"rank{rank}{mode}.npz"), first=results[0],
+                 second=results[1])
     finally:
         dist.destroy_process_group()
 
@@ -98,8 +102,13 @@ def _host_result(name, inputs, p):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("name", ["matmul", "attention", "softmax", "rmsnorm"])
-def test_fused_gather_on_two_gpus(tmp_path, name):
+@pytest.mark.parametrize("name,mode", [("matmul", "fused"), ("attention", "fused"),
+                                       ("softmax", "fused"), ("rmsnorm", "fused"),
+                                       ("softmax", "copy"), ("rmsnorm", "copy")])
+def test_fused_gather_on_two_gpus(tmp_path, name, mode):
+    """``fused``: the kernels' epilogues store into both ranks' outputs;
+    ``copy``: the kernels write this rank's rows of its own full output (two
+    row blocks) and the copy engines move them into the peer's."""
     import torch
     import torch.multiprocessing as mp
     from emmy_ptx import workloads
@@ -108,7 +117,7 @@ def test_fused_gather_on_two_gpus(tmp_path, name):
         pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), name))
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, str(tmp_path), name, mode))
              for r in range(2)]
     for p in procs:
         p.start()
@@ -124,7 +133,7 @@ def test_fused_gather_on_two_gpus(tmp_path, name):
     inputs = full.make_inputs()
     want = _host_result(name, inputs, full)
     for r in range(2):
-        got = np.load(tmp_path / f"rank{r}.npz")
+        got = np.load(tmp_path / f"rank{r}{mode}.npz")
         for k in ("first", "second"):
             ok, msg = check_close(name, f"{name} rank {r} {k}", got[k], want, inputs)
             assert ok, msg
