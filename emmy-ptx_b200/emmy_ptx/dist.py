@@ -337,43 +337,50 @@ class FusedGather:
 
 
 class CopyGather:
-    """Rank ``rank``'s shard of a row problem ("rmsnorm", "softmax", ...)
-    whose output all-gather runs on the copy engines: the shard's kernel
-    writes its rows straight into this rank's full output (``out.local``, at
-    the shard's row offset), then one device-to-device copy per peer
-    (``ert_memcpy_dtod`` into the peer's full output, mapped with CUDA IPC)
-    moves them over NVLink, one stream per peer so the copies run on several
-    engines at once.  With ``chunks`` > 1 the shard runs as that many row
-    blocks, and a block's copies overlap the next block's kernel.  After
-    ``launch()`` and ``wait()`` on every rank, ``out.local`` holds the full
-    output everywhere."""
+    """Rank ``rank``'s shard of ``name`` whose output all-gather runs on the
+    copy engines.  Every partition with a contiguous, rank-major output
+    (rows, row blocks of C, (batch x head) pairs) works: the shard's kernel
+    writes straight into this rank's part of its full output (``out.local``),
+    then one device-to-device copy per peer (``ert_memcpy_dtod`` into the
+    peer's full output, mapped with CUDA IPC) moves it over NVLink, one
+    stream per peer so the copies run on several engines at once.  With
+    ``chunks`` > 1 the shard runs as that many sub-shards (separate
+    launches), and a sub-shard's copies overlap the next one's kernel.
+    After ``launch()`` and ``wait()`` on every rank, ``out.local`` holds the
+    full output everywhere."""
 
     def __init__(self, name: str, rank: int, world: int, workdir, chunks: int = 1,
                  group=None, **kw):
         from .runtime import Event, Kernel, Stream
-        if PARTITION[name] != "rows":
-            raise ValueError(f"{name} is not partitioned by rows")
+        if PARTITION[name] == "cols":
+            raise ValueError(f"{name}'s output is not rank-major contiguous")
         self.name, self.rank, self.world, self.group = name, rank, world, group
         self.part, self.full = shard_problem(name, rank, world, **kw)
-        sub, _ = shard_problem(name, rank * chunks, world * chunks, **kw)
+        self.sub, _ = shard_problem(name, rank * chunks, world * chunks, **kw)
         self.chunks = chunks
-        self.kernel = Kernel.from_ir(sub.write(os.path.join(workdir, f"copyg_{name}_{rank}")))
+        self.kernel = Kernel.from_ir(self.sub.write(os.path.join(workdir,
+                                                                 f"copyg_{name}_{rank}")))
+        # one module per sub-shard: a tensor-map kernel keeps its maps in
+        # module globals, so each sub-shard's launch has its own
+        self.kernels = [self.kernel] + [
+            Kernel(self.kernel.ptx, self.kernel.entry, self.kernel.args,
+                   self.kernel.meta_geom, self.kernel.sidecar) for _ in range(chunks - 1)]
         out = self.part.outputs[0]
         self.out_name = out
-        self.row_bytes = self.full["cols"] * 4
-        self.rows = self.part.tensor(out)["shape"][0]          # this rank's rows
-        self.sub_rows = sub.tensor(out)["shape"][0]
-        self.row0 = rank * self.rows
-        self.out = PeerBuffer(self.full["rows"] * self.row_bytes, group)
+        numel = lambda p, t: int(np.prod(p.tensor(t)["shape"]))  # noqa: E731
+        self.sub_bytes = numel(self.sub, out) * 4
+        self.part_bytes = numel(self.part, out) * 4
+        self.out = PeerBuffer(self.part_bytes * world, group)
         self.copy_streams = [Stream() for _ in range(world)]
         self.k_done = [Event() for _ in range(chunks)]
         self.c_done = [Event() for _ in range(world)]
         self._launches = None
 
     def bind(self, buffers: dict, stream=None):
-        """``buffers``: the shard's inputs (this rank's rows; their row-split
-        tensors are cut into the chunks here).  The output argument is this
-        rank's rows of ``out.local``."""
+        """``buffers``: the shard's inputs; an input that the sub-shards
+        split (its sub-shard shape differs from the shard's) is cut into
+        consecutive blocks, the others are shared.  The output argument is
+        this rank's part of ``out.local``."""
         from .runtime import _stream_handle
         self.stream = _stream_handle(stream)
         self._launches = []
@@ -381,26 +388,24 @@ class CopyGather:
             bufs = {}
             for t in self.part.inputs:
                 ten = buffers[t]
-                split = self.part.tensor(t)["shape"][0] == self.rows and \
-                    len(self.part.tensor(t)["shape"]) > 1
                 ptr = ten.data_ptr() if hasattr(ten, "data_ptr") else int(ten)
-                if split:
-                    ptr += c * self.sub_rows * self.part.tensor(t)["shape"][1] * \
-                        ten.element_size()
+                if self.sub.tensor(t)["shape"] != self.part.tensor(t)["shape"]:
+                    esz = ten.element_size() if hasattr(ten, "element_size") else 4
+                    ptr += c * int(np.prod(self.sub.tensor(t)["shape"])) * esz
                 bufs[t] = ptr
-            bufs[self.out_name] = self.out.local.ptr + (self.row0 + c * self.sub_rows) * \
-                self.row_bytes
-            self._launches.append(self.kernel.bind(bufs, stream=self.stream))
+            bufs[self.out_name] = (self.out.local.ptr + self.rank * self.part_bytes
+                                   + c * self.sub_bytes)
+            self._launches.append(self.kernels[c].bind(bufs, stream=self.stream))
         return self
 
     def launch(self):
         from .runtime import check, lib
         L = lib()
-        nbytes = self.sub_rows * self.row_bytes
+        nbytes = self.sub_bytes
         for c, launch in enumerate(self._launches):
             launch()
             self.k_done[c].record(self.stream)
-            off = (self.row0 + c * self.sub_rows) * self.row_bytes
+            off = self.rank * self.part_bytes + c * self.sub_bytes
             for i in range(1, self.world):
                 d = (self.rank + i) % self.world
                 cs = self.copy_streams[d]
@@ -427,6 +432,8 @@ class CopyGather:
     def close(self):
         for s in self.copy_streams:
             s.synchronize()
+        for k in self.kernels:
+            k.free_scratch()
         self.out.close()
         for s in self.copy_streams:
             s.destroy()
@@ -499,6 +506,20 @@ def bench_fused_gather(name, workdir, device, stream, rank, world, steps=5, warm
     torch.cuda.synchronize()
     fused.close()
     plain.free_scratch()
+    # the copy engines instead: two sub-shard launches, each followed by one
+    # copy per peer
+    copy = CopyGather(name, rank, world, workdir, chunks=2, **kw).bind(dev, stream=stream)
+
+    def copy_step():
+        with torch.cuda.stream(stream):
+            copy.launch()
+            copy.wait()
+
+    ms = run(copy_step)
+    res["copy_gather_incl_ms"] = round(ms, 4)
+    res["copy_gather_incl_tflops"] = round(flops / ms / 1e9, 1)
+    torch.cuda.synchronize()
+    copy.close()
     if name == "matmul":
         res["partition"] = (f"row blocks of C ({full['m'] // world} of {full['m']} rows per rank, "
                             "B replicated)")

@@ -426,7 +426,7 @@ class Kernel:
                 values.append(ctypes.c_uint64(p))
         ptrs.update(self._scratch_ptrs())
         self._prepare_tensormaps(ptrs, s)
-        main = BoundLaunch(self, values, self.geometry(geometry), s)
+        main = BoundLaunch(self, values, self.geometry(geometry), s, tmap_ptrs=ptrs)
         pre = []
         for aux in self.sidecar.get("prelaunch") or []:
             fn = self.module.function(aux["entry"])
@@ -483,7 +483,7 @@ class BoundLaunch:
     """A kernel launch with its arguments marshalled (see Kernel.bind)."""
 
     def __init__(self, kernel: Kernel, values: list, geom: ErtGeom, stream: int,
-                 function: int | None = None):
+                 function: int | None = None, tmap_ptrs: dict | None = None):
         self.kernel = kernel
         self.values = values          # keeps the ctypes values alive
         self.argv = (ctypes.c_void_p * len(values))(
@@ -492,8 +492,19 @@ class BoundLaunch:
         self.stream = stream
         self._launch = lib().ert_launch
         self._fn = kernel.function if function is None else function
+        # the tensor maps live in the module's globals, shared by every bind
+        # of the kernel: a launch whose buffers differ from the last bind's
+        # writes its own maps again first (stream-ordered, so earlier
+        # launches still read theirs)
+        maps = kernel.sidecar.get("tensormaps") or []
+        self._tmap_ptrs = tmap_ptrs if maps and tmap_ptrs is not None else None
+        self._tmap_key = (tuple(tmap_ptrs.get(m["arg"]) for m in maps)
+                          if self._tmap_ptrs is not None else None)
 
     def __call__(self):
+        if self._tmap_ptrs is not None and \
+                self.kernel._tmap_cache.get("key") != self._tmap_key:
+            self.kernel._prepare_tensormaps(self._tmap_ptrs, self.stream)
         rc = self._launch(self._fn, ctypes.byref(self.geom), self.argv, self.stream)
         if rc != 0:
             check(rc, f"launch of {self.kernel.entry}")

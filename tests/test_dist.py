@@ -188,3 +188,31 @@ def test_peer_buffer_tables_are_rank_ordered(tmp_path):
         assert d["ptrs"] == want
         assert sorted(d["closed"]) == sorted(p for o, p in enumerate(want) if o != r)
         assert d["freed"]
+
+
+def test_copy_gather_offsets_cover_the_output_once():
+    """The copy-engine gather's sub-shards: for every partition with a
+    rank-major contiguous output, rank r's chunk c lands at
+    r * part + c * sub bytes, and the chunks of all ranks tile the full
+    output exactly once (checked on the shapes alone, no device)."""
+    from emmy_ptx import dist as edist
+    for name, kw in [("softmax", dict(rows=64, cols=256)), ("rmsnorm", dict(rows=32, cols=128)),
+                     ("matmul", dict(m=512, n=128, k=64)),
+                     ("attention", dict(batch=2, heads=4, seq=64, head_dim=32))]:
+        world, chunks = 2, 2
+        full = edist.workloads.build(name, **kw)
+        out = full.outputs[0]
+        total = int(np.prod(full.tensor(out)["shape"])) * 4
+        spans = []
+        for r in range(world):
+            part, _ = edist.shard_problem(name, r, world, **kw)
+            sub, _ = edist.shard_problem(name, r * chunks, world * chunks, **kw)
+            pb = int(np.prod(part.tensor(out)["shape"])) * 4
+            sb = int(np.prod(sub.tensor(out)["shape"])) * 4
+            assert pb == chunks * sb and world * pb == total, name
+            spans += [(r * pb + c * sb, sb) for c in range(chunks)]
+        pos = 0
+        for off, n in sorted(spans):
+            assert off == pos, name
+            pos += n
+        assert pos == total, name

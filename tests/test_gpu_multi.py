@@ -104,7 +104,8 @@ def _host_result(name, inputs, p):
 @pytest.mark.gpu
 @pytest.mark.parametrize("name,mode", [("matmul", "fused"), ("attention", "fused"),
                                        ("softmax", "fused"), ("rmsnorm", "fused"),
-                                       ("softmax", "copy"), ("rmsnorm", "copy")])
+                                       ("softmax", "copy"), ("rmsnorm", "copy"),
+                                       ("matmul", "copy"), ("attention", "copy")])
 def test_fused_gather_on_two_gpus(tmp_path, name, mode):
     """``fused``: the kernels' epilogues store into both ranks' outputs;
     ``copy``: the kernels write this rank's rows of its own full output (two
