@@ -110,3 +110,35 @@ def test_chunked_host_pipeline_matches_oracle(cuda, name, kw, tmp_path):
             ok, msg = check_close(p.category, o, outs[o].array, want[o], inputs)
             assert ok, f"call {call + 1}: {msg}"
     r.free()
+
+
+@pytest.mark.gpu
+def test_two_binds_of_a_tensor_map_kernel_keep_their_own_buffers(cuda):
+    """A tensor-map kernel keeps its TMA descriptors in module globals that
+    every bind shares.  Two binds on different buffers, launched in the
+    order first, second, first, each compute on their own buffers (the
+    runtime writes a launch's maps again when another bind replaced them)."""
+    import numpy as np
+    import torch
+    from emmy_ptx import workloads
+    from emmy_ptx.runtime import Kernel
+    p = workloads.build("matmul", m=256, n=256, k=128)
+    with tempfile.TemporaryDirectory() as td:
+        kern = Kernel.from_ir(p.write(td))
+    assert kern.sidecar.get("tensormaps")
+    sets, launches = [], []
+    for seed in (1, 2):
+        host = p.make_inputs(seed=seed)
+        dev = {n: torch.from_numpy(v).to(cuda) for n, v in host.items()}
+        dev["C"] = torch.full((256, 256), float("nan"), device=cuda)
+        sets.append((host, dev))
+        launches.append(kern.bind(dev))
+    for i in (0, 1, 0):
+        sets[i][1]["C"].fill_(float("nan"))
+        launches[i]()
+        torch.cuda.synchronize()
+        host, dev = sets[i]
+        want = host["A"].astype(np.float64) @ host["B"].astype(np.float64)
+        ok, msg = check_close("matmul", f"C of bind {i}", dev["C"].cpu().numpy(), want, host)
+        assert ok, msg
+    assert kern.status() == 0
