@@ -23,9 +23,10 @@
 // Set-up: the first call on a device (with that device's context current)
 // resolves the array's address with cudaGetSymbolAddress and caches it; with
 // lazy module loading that is also when the library's device image, and with
-// it the array, is loaded onto the device.  Make that first call before any
-// stream capture begins.  Nothing in the scratch
-// has to start at zero: the pre-pass writes every byte the attention kernel
+// it the array, is loaded onto the device.  No call can be recorded into a
+// CUDA graph: each copies its tensor maps from a pageable host buffer, which
+// stream capture does not allow.  Nothing in the scratch has to start at
+// zero: the pre-pass writes every byte the attention kernel
 // reads, and the tensor maps zero-fill rows past the sequence end.
 //
 // Calls share one scratch array and rewrite the module's three tensor-map

@@ -47,7 +47,9 @@ extern "C" {
  * Allocates nothing.  The first call on a device resolves the array's
  * address (once per device, with that device's context current; under lazy
  * module loading this also loads the library's device image, and with it the
- * array); make that call before any stream capture starts.  Returns
+ * array).  A call cannot be recorded into a CUDA graph: it copies the three
+ * tensor maps from a pageable host buffer, which stream capture does not
+ * allow, so issue it outside any capture.  Returns
  * ERT_E_TOO_LARGE, without launching, when
  * 2 * align256(heads_total*seq*head_dim*4) exceeds ERT_NOALLOC_SCRATCH_BYTES,
  * and ERT_E_ARGUMENT, without launching, when heads_total/seq/head_dim is not
