@@ -237,13 +237,16 @@ def link_probe(device, h2d_bytes, d2h_bytes, barrier, max_over_ranks, reps=3):
     return best, mine
 
 
-def e2e_measure(names, workdir, steps, warmup, seed_offset, chunks=16, slots=3, rows_div=1):
+def e2e_measure(names, workdir, steps, warmup, seed_offset, chunks=16, slots=3, rows_div=1,
+                barrier=None):
     """The same step through the public host-buffer API: pinned host inputs
     -> device, the kernels, device -> pinned host outputs, every step.  Rows
     are cut into ``chunks`` blocks; copy-in, kernels and copy-out run on three
     streams of the C ABI, ordered per device slot by events
     (emmy_ptx.pipeline), and the problems share the streams so one step's
-    copies never drain the link between problems."""
+    copies never drain the link between problems.  ``barrier`` (several
+    ranks): called after the warm-up, so that every rank's timed steps run
+    at the same time and share the host links as they would in a job."""
     from emmy_ptx.pipeline import ChunkedHostRunner, PipelineStreams
     from emmy_ptx.runtime import Event, PinnedArray
     ps = PipelineStreams()
@@ -270,6 +273,8 @@ def e2e_measure(names, workdir, steps, warmup, seed_offset, chunks=16, slots=3, 
         for r, host, outs in runners:
             r.run(host, outs, sync=False)
     ps.synchronize()
+    if barrier is not None:
+        barrier()
     start, end = Event(), Event()
     marks = [Event() for _ in range(3)]
     start.record(ps.h2d)
@@ -661,7 +666,7 @@ def run_b200(args):
     chunks = 16
     barrier()
     e2e = e2e_measure(HEADLINE, workdir, max(3, args.steps // 4), 2, rank,
-                      chunks=chunks, rows_div=world)
+                      chunks=chunks, rows_div=world, barrier=barrier)
     et = max_over_ranks(e2e["ms_per_step"])
     e2e_value = world * e2e["bytes"] / et / 1e6
     # the same copies with no kernels, all ranks at once: the step's ceiling

@@ -296,6 +296,90 @@ def pointwise_mixed(rows=16, cols=64, block=256) -> Problem:
                    _grid_for(rows * cols // 4, block), (block, 1, 1), seed=6)
 
 
+def bit_ops(rows=16, cols=64, block=256) -> Problem:
+    """Bit-level and sign-sensitive elementwise ops, one output each:
+    ``bitcast`` both ways between f32 and int32 (the bits move, the value
+    is not converted; compiler.py:1276-1295), ``pad`` (a plain copy,
+    1271-1274), ``pow`` of a signed base (an odd integer exponent keeps the
+    sign, a non-integer one gives NaN; 946-1010), ``xor`` and shifts whose
+    count runs past 31 (``shl.b32`` / ``shr.s32`` clamp the count;
+    1374-1404)."""
+    assert cols % 4 == 0
+    idx = (V("a0"), mul(V("a1"), 4))
+    x, e, n, s = _names("x", 4), _names("e", 4), _names("n", 4), _names("s", 4)
+    body = [Load(x, "x", idx, F32), Load(e, "e", idx, F32), Load(n, "n", idx, S32),
+            Load(s, "s", idx, S32)]
+    for k in range(4):
+        body += [_assign(f"b__u{k}", "bitcast", (x[k],), S32),
+                 _assign(f"f__u{k}", "bitcast", (n[k],), F32),
+                 _assign(f"p__u{k}", "pad", (x[k],), F32),
+                 _assign(f"w__u{k}", "pow", (x[k], e[k]), F32),
+                 _assign(f"x__u{k}", "xor", (n[k], s[k]), S32),
+                 _assign(f"l__u{k}", "left_shift", (n[k], s[k]), S32),
+                 _assign(f"r__u{k}", "right_shift", (n[k], s[k]), S32)]
+    outs = {"o_bits": ("b", S32), "o_float": ("f", F32), "o_pad": ("p", F32),
+            "o_pow": ("w", F32), "o_xor": ("x", S32), "o_shl": ("l", S32),
+            "o_shr": ("r", S32)}
+    for o, (pre, dt) in outs.items():
+        body.append(Write(o, idx, tuple(f"{pre}__u{k}" for k in range(4)), dt, False, "NONE"))
+    tile = Tile((Axis("a0", Dim(rows)), Axis("a1", Dim(cols // 4))), tuple(body),
+                block_threads=block)
+    k = KernelOp("k_bit_ops_pointwise", ("x", "e", "n", "s"), tuple(outs), (tile,))
+    shape = (rows, cols)
+    return Problem("bit_ops", "bit_ops", k,
+                   [_t("x", shape, "f32"), _t("e", shape, "f32"), _t("n", shape, "s32"),
+                    _t("s", shape, "s32")]
+                   + [_t(o, shape, "s32" if dt is S32 else "f32") for o, (_, dt) in outs.items()],
+                   _grid_for(rows * cols // 4, block), (block, 1, 1), seed=9)
+
+
+def offset_copy(rows=8, cols=64, offset=1, pad=4, block=128) -> Problem:
+    """out[r, 4c + k] = 2 * x[r, 4c + k + offset] for k < 4, with x of shape
+    [rows, cols + pad] and out [rows, cols].  The grouped 4-wide load is
+    aligned only when ``offset`` and the row length ``cols + pad`` are both
+    multiples of 4; otherwise it must stay four scalar loads (the
+    reference's vectorisation rules, compiler.py:1587-1719).  The write is
+    always aligned."""
+    assert cols % 4 == 0 and 0 <= offset <= pad
+    src = (V("a0"), add(mul(V("a1"), 4), offset))
+    dst = (V("a0"), mul(V("a1"), 4))
+    x = _names("x", 4)
+    body = [Load(x, "x", src, F32), Let("two", Lf(2.0), F32)]
+    for k in range(4):
+        body.append(_assign(f"o__u{k}", "multiply", (x[k], "two")))
+    body.append(Write("out", dst, _names("o", 4), F32, False, "NONE"))
+    tile = Tile((Axis("a0", Dim(rows)), Axis("a1", Dim(cols // 4))), tuple(body),
+                block_threads=block)
+    k = KernelOp("k_offset_copy", ("x",), ("out",), (tile,))
+    return Problem("offset_copy", "offset_copy", k,
+                   [_t("x", (rows, cols + pad), "f32"), _t("out", (rows, cols), "f32")],
+                   _grid_for(rows * cols // 4, block), (block, 1, 1), seed=11,
+                   params={"offset": offset})
+
+
+def rowsum_f64(rows=64, cols=512, threads=128) -> Problem:
+    """out[r] = sum over c of x[r, c] in f64: pairs of f64 loads, the warp
+    butterfly on f64 values (two 32-bit halves per shuffle, compiler.py:
+    1877-1928) and the shared-memory tree over the warps."""
+    assert cols % 2 == 0 and threads % 32 == 0
+    a = _names("a", 2)
+    loop = StridedLoop(
+        Axis("c", Dim(cols // 2)), V("t"), L(threads),
+        (Load(a, "x", (V("r"), mul(V("c"), 2)), F64),
+         *[Accum("acc", red("sum"), None, a[k], F64, ("c",)) for k in range(2)]),
+        False, None, True)
+    body = (Smem("red_smem", (threads // 32,), F64, 8), loop,
+            *_warp_tree("acc", "sum", F64, "red_smem", threads),
+            Cond(BinaryExpr("==", V("t"), L(0)),
+                 (Write("out", (V("r"),), ("acc",), F64, False, "NONE"),), ()))
+    tile = Tile((Axis("r", Dim(rows)), Axis("t", Dim(threads))), body,
+                block_threads=threads)
+    k = KernelOp("k_rowsum_f64", ("x",), ("out",), (tile,))
+    return Problem("rowsum_f64", "rowsum_f64", k,
+                   [_t("x", (rows, cols), "f64"), _t("out", (rows,), "f64")],
+                   (rows, 1, 1), (threads, 1, 1), seed=10)
+
+
 # -- config 2: fused row kernels ---------------------------------------------
 def rmsnorm(rows=8192, cols=4096, threads=256, eps=1e-6) -> Problem:
     """out = x * rsqrt(mean(x^2) + eps) * w, one block per row."""
@@ -822,6 +906,35 @@ def _in_mixed(p, seed):
     return {"d": d.numpy(), "f": f.numpy(), "n": n.numpy()}
 
 
+def _in_bit_ops(p, seed):
+    """x ~ N(0, 4); exponents: integers in [-3, 3], a quarter of them moved
+    to the half-integer above; n: int32 bit patterns of finite floats (an
+    all-ones exponent field loses its lowest bit); shift counts in [0, 40]."""
+    import torch
+    g = _gen(seed)
+    sh = _shape(p, "x")
+    x = torch.randn(sh, generator=g) * 2
+    e = torch.randint(-3, 4, sh, generator=g).float()
+    e = e + 0.5 * (torch.rand(sh, generator=g) < 0.25).float()
+    n = torch.randint(-2**31, 2**31, sh, generator=g, dtype=torch.int64)
+    n = torch.where((n & 0x7F800000) == 0x7F800000, n ^ 0x00800000, n).to(torch.int32)
+    s = torch.randint(0, 41, sh, generator=g, dtype=torch.int32)
+    return {"x": x.numpy(), "e": e.numpy(), "n": n.numpy(), "s": s.numpy()}
+
+
+def _in_offset_copy(p, seed):
+    import torch
+    g = _gen(seed)
+    return {"x": torch.randn(_shape(p, "x"), generator=g).numpy()}
+
+
+def _in_rowsum_f64(p, seed):
+    import torch
+    g = _gen(seed)
+    x = torch.rand(_shape(p, "x"), generator=g, dtype=torch.float64) * 2 - 1
+    return {"x": x.numpy()}
+
+
 def _in_rmsnorm(p, seed):
     import torch
     g = _gen(seed)
@@ -914,6 +1027,9 @@ _INPUT_RECIPES = {
     "control_flow": _in_control,
     "pointwise_zoo": _in_zoo,
     "pointwise_mixed": _in_mixed,
+    "bit_ops": _in_bit_ops,
+    "rowsum_f64": _in_rowsum_f64,
+    "offset_copy": _in_offset_copy,
     "pointwise_f32": _in_pointwise_f32,
     "pointwise_i32": _in_pointwise_i32,
     "rmsnorm": _in_rmsnorm,
@@ -935,6 +1051,9 @@ BUILDERS = {
     "control_flow": control_flow,
     "pointwise_zoo": pointwise_zoo,
     "pointwise_mixed": pointwise_mixed,
+    "bit_ops": bit_ops,
+    "rowsum_f64": rowsum_f64,
+    "offset_copy": offset_copy,
     "pointwise_f32": pointwise_f32,
     "pointwise_i32": pointwise_i32,
     "rmsnorm": rmsnorm,

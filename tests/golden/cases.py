@@ -30,6 +30,12 @@ PARITY = {
                                                         causal=False)),
     "pointwise_zoo_16x64": ("pointwise_zoo", dict(rows=16, cols=64)),
     "pointwise_mixed_16x64": ("pointwise_mixed", dict(rows=16, cols=64)),
+    "bit_ops_16x64": ("bit_ops", dict(rows=16, cols=64)),
+    "bit_ops_7x36": ("bit_ops", dict(rows=7, cols=36)),
+    "rowsum_f64_9x300": ("rowsum_f64", dict(rows=9, cols=300)),
+    "rowsum_f64_64x512": ("rowsum_f64", dict(rows=64, cols=512)),
+    "offset_copy_8x64_o1": ("offset_copy", dict(rows=8, cols=64, offset=1, pad=4)),
+    "offset_copy_5x68_p2": ("offset_copy", dict(rows=5, cols=68, offset=0, pad=2)),
 }
 
 FULL = {

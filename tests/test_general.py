@@ -20,7 +20,8 @@ SMALL = {"pointwise_f32": dict(rows=33, cols=100), "pointwise_i32": dict(rows=33
          "pointwise_zoo": dict(rows=16, cols=64), "pointwise_mixed": dict(rows=16, cols=64),
          "histogram_i32": dict(rows=16, cols=100, bins=13), "control_flow": dict(n=300),
          "matmul_bf16": dict(m=128, n=128, k=64), "matmul_e4m3": dict(m=128, n=128, k=128),
-         "matmul_e5m2": dict(m=128, n=128, k=128)}
+         "matmul_e5m2": dict(m=128, n=128, k=128), "bit_ops": dict(rows=7, cols=36),
+         "rowsum_f64": dict(rows=9, cols=300), "offset_copy": dict(rows=5, cols=68, offset=0, pad=2)}
 
 
 def _comp(name, tmp_path, target="sm_100a", version="8.7", **kw):
@@ -75,6 +76,38 @@ def test_vector_and_read_only_loads(tmp_path):
     _, comp = _comp("pointwise_f32", tmp_path, rows=64, cols=256)
     ptx, _ = general.emit(comp)
     assert "ld.global.nc.v4.f32" in ptx and "st.global.v4.f32" in ptx
+
+
+@pytest.mark.parametrize("offset,pad,vector", [(4, 4, True), (1, 4, False), (2, 4, False),
+                                               (0, 2, False), (0, 4, True)])
+def test_grouped_load_is_a_vector_only_when_aligned(tmp_path, offset, pad, vector):
+    """A 4-wide group becomes one 16-byte access only when its first
+    element is provably 16-byte aligned: the column offset and the row
+    length both multiples of 4 (reference tests/test_compiler.py:101-203).
+    Anything else stays four scalar accesses, which the GPU requires."""
+    _, comp = _comp("offset_copy", tmp_path, rows=8, cols=64, offset=offset, pad=pad)
+    ptx, _ = general.emit(comp)
+    assert ("ld.global.nc.v4.f32" in ptx) == vector
+    assert ("ld.global.nc.f32" in ptx) == (not vector)
+    assert "st.global.v4.f32" in ptx
+
+
+def test_atomic_grouped_write_stays_scalar(tmp_path):
+    """Atomic writes of a group are one reduction per element."""
+    from emmy_ptx.ir import F32, Axis, Dim, KernelOp, Load, Tile, Write
+    from emmy_ptx.workloads import Problem, V, _names, _t, mul
+    idx = (V("a0"), mul(V("a1"), 4))
+    x = _names("x", 4)
+    tile = Tile((Axis("a0", Dim(4)), Axis("a1", Dim(8))),
+                (Load(x, "x", idx, F32), Write("out", idx, x, F32, True, "NONE")),
+                block_threads=32)
+    p = Problem("atomic_add", "atomic_add", KernelOp("k_atomic_add", ("x",), ("out",), (tile,)),
+                [_t("x", (4, 32), "f32"), _t("out", (4, 32), "f32")], (1, 1, 1), (32, 1, 1), 0)
+    comp = Compiler(p.write(tmp_path / "atomic"), target="sm_100a", ptx_version="8.7")
+    ptx, _ = general.emit(comp)
+    assert "red.global.add.f32" in ptx or "atom.global.add.f32" in ptx
+    assert ".v4" not in "\n".join(line for line in ptx.splitlines() if "red." in line or "atom." in line)
+    assert "st.global.v4" not in ptx
 
 
 def test_a_value_assigned_in_both_branches_is_one_register(tmp_path):

@@ -14,7 +14,7 @@ from tolerances import check_close
 GOLDEN = Path(__file__).resolve().parent / "golden" / "problems"
 
 LOWERED = {"pointwise_zoo", "pointwise_mixed", "pointwise_f32", "pointwise_i32", "rmsnorm", "softmax", "rowsum_i32", "matmul", "attention",
-           "colreduce_f64"}
+           "colreduce_f64", "bit_ops", "rowsum_f64", "offset_copy"}
 
 PARITY = [t for t, (name, _) in cases.PARITY.items() if name in LOWERED]
 

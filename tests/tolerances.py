@@ -5,6 +5,8 @@ f32 pointwise:   |a - b| <= 1e-5 * max(|b|, 1)
 f32 RMSNorm:     |a - b| <= 1e-5 * max(|b|, 1e-3)
 f32 softmax:     |a - b| <= 1e-5 * max(|b|, 1/cols)
 f64 col sum:     |a - b| <= 1e-12 * sum_i |x_i| (per column); col max exact
+f64 row sum:     |a - b| <= 1e-12 * sum_j |x_j| (per row)
+bit ops:         bitcast, pad: bit-exact; pow: |a - b| <= 1e-5 * max(|b|, 1)
 f32 matmul (3xTF32 on tcgen05), and bf16/f16 matmul into f32:
                  |a - b| <= 1e-3 * (|b| + ||A_i|| * ||B_j|| / sqrt(K))
 f32 attention:   |a - b| <= 1e-3 * (|b| + max_j |v_j| / sqrt(keys attended))
@@ -56,6 +58,10 @@ def check_close(category, name, got, want, inputs=None, causal=True):
             tol = np.zeros_like(b)
         else:
             tol = 1e-12 * np.abs(inputs["x"]).sum(0)
+    elif category == "rowsum_f64":
+        tol = 1e-12 * np.abs(inputs["x"]).sum(1)
+    elif category == "bit_ops":
+        tol = 1e-5 * np.maximum(b, 1.0) if name == "o_pow" else np.zeros_like(b)
     elif category in ("matmul", "matmul_lowp"):
         A, B = (as_float(inputs[n]) for n in ("A", "B"))
         na = np.linalg.norm(A, axis=1)[:, None]
