@@ -13,11 +13,13 @@ Inputs (2.4 GB per step) are larger than the 126 MB L2, so no flush is
 needed between steps.
 
 N > 1 (torchrun): strong scaling, the north star's sharded path -- every
-rank runs its 1/N of the rows of both kernels, then NCCL
-``all_gather_into_tensor`` puts both full outputs on every rank, inside
-the timed step (max over ranks).  The kernel-only time and the matmul /
-attention shards (NCCL gather vs the fused epilogue gather) are reported
-under ``"sharded"``.
+rank runs its 1/N of the rows of both kernels, and both full outputs are on
+every rank at the end of the timed step (max over ranks).  The exchange is
+``GATHER_MODE``: by default the row kernels' gather variant stores every
+output row into every rank's output over NVLink.  The same step with NCCL
+``all_gather_into_tensor``, with the copy-engine gather, and with the
+kernels alone, and the matmul / attention shards (NCCL, copy-engine and
+fused epilogue gathers), are reported under ``"sharded"``.
 
 ``e2e`` is the same config through the host-buffer pipeline of the C ABI
 (pinned host rows -> device -> kernels -> pinned host, every step; each
@@ -437,8 +439,10 @@ class HeadlineStep:
     the step.  ``gather="fused"``: the row kernels' gather variant stores
     every output row into every rank's full output over NVLink
     (dist.FusedGather), then a one-element NCCL all-reduce on the stream
-    marks completion; ``gather="nccl"``: the plain kernels, then NCCL
-    all_gather_into_tensor of every output."""
+    marks completion; ``gather="copy"``: the kernels into this rank's part
+    of its full output, copy engines to the peers (dist.CopyGather);
+    ``gather="nccl"``: the plain kernels, then NCCL all_gather_into_tensor of
+    every output."""
 
     def __init__(self, workdir, device, stream, rank, world, gather="fused"):
         import torch
