@@ -26,8 +26,10 @@
 // it the array, is loaded onto the device.  No call can be recorded into a
 // CUDA graph: each copies its tensor maps from a pageable host buffer, which
 // stream capture does not allow.  Nothing in the scratch has to start at
-// zero: the pre-pass writes every byte the attention kernel
-// reads, and the tensor maps zero-fill rows past the sequence end.
+// zero: the pre-pass (head group 0) and the kernel's split warp (the later
+// groups) write every byte the attention kernel reads, and the tensor maps
+// zero-fill rows past the sequence end.  The pre-pass also records the two
+// scratch addresses for the split warp, so it runs before every launch.
 //
 // Calls share one scratch array and rewrite the module's three tensor-map
 // globals, so two calls that overlap in time (different streams, or threads

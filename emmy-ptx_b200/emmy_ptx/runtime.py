@@ -324,12 +324,28 @@ class Kernel:
         self.sidecar = sidecar or {}
         self.module = Module(ptx)
         self.function = self.module.function(entry)
+        self._check_register_split()
         self._tmap_cache: dict = {}
         self.launches = 0
         # scratch buffers the kernel needs beyond its arguments (sidecar
         # "scratch": [{"name", "bytes"}]); allocated on first bind, freed
         # with the kernel
         self.scratch: dict = {}
+
+    def _check_register_split(self):
+        """A kernel whose warpgroups re-divide their registers
+        (``setmaxnreg``, sidecar ``register_split``) must have been given the
+        launch register count the split assumes: ``setmaxnreg.inc`` beyond
+        the block's registers waits forever.  Refuse it before any launch."""
+        rs = self.sidecar.get("register_split")
+        if not rs:
+            return
+        have = self.module.attrs(self.entry)["num_regs"]
+        for threads, need in rs["registers_by_block"].items():
+            if have < rs["launch"] or need > int(threads) * have:
+                raise EmmyRuntimeError(
+                    f"{self.entry}: {have} registers per thread at launch; its register "
+                    f"split needs {rs['launch']} ({need} registers over {threads} threads)")
 
     # -- construction ----------------------------------------------------
     @staticmethod

@@ -24,7 +24,15 @@ the others:
   every query tile of the
   head, so doing this in the attention kernel would repeat the work S/128
   times; the tensor core drops the low 13 bits of an f32 operand, so an
-  unrounded V would bias every product towards zero).
+  unrounded V would bias every product towards zero).  With more than one
+  head group the pre-pass covers group 0 only, and warp 8 of the kernel
+  writes the later groups while the other warps compute: it takes chunks
+  (up to 128 per group) from a counter in global memory and releases each
+  on its group's count, which the producers acquire before their first
+  load of a group's K lo / rounded V.  The 288-thread launch has 168
+  registers per thread; warps 0-3 raise theirs to 224 and warps 4-7 lower
+  theirs to 96 (``setmaxnreg``).  On a 256-thread launch (the meta.json
+  block) every warp splits first and then takes its role.
 * warps 0-3 (softmax): thread r owns query row r of the tile.  It loads its
   Q row, folds in scale * log2(e), splits it into tf32 hi/lo, stores hi into
   TMEM and lo into shared memory (the A operands of S = Q K^T, which is
@@ -62,7 +70,7 @@ from .. import ir as I
 from .common import NoMatch, declare_params, launch_block
 from .ops import dtype_name
 from .ptx import KernelBuilder, f32_hex, wide_vectors
-from .tc import TC, idesc_tf32, smem_desc_hi, split_launch
+from .tc import STATUS_NO_PREPASS, STATUS_TIMEOUT, TC, idesc_tf32, smem_desc_hi, split_launch
 
 BQ = 128           # queries per tile (TMEM lanes)
 BKV = 128          # keys per S tile (the N of each QK^T MMA)
@@ -82,6 +90,21 @@ ROLE_SOFTMAX, ROLE_PRODUCER, ROLE_MMA = 5, 6, 7
 # arrivals of the softmax warps on the barriers the MMA issuers wait on (P
 # ready, Q ready): 4 = one per warp, 128 = one per thread
 ARRIVALS = 4
+# K's lo part and the rounded V of every head group but the first are
+# written inside the kernel, by a ninth warp that takes chunks of the work
+# from a shared counter while the other warps compute; the pre-pass then
+# covers group 0 only.  (CTA pairs keep the whole pre-pass.)
+INLINE_SPLIT = True
+SPLIT_CHUNKS = 128         # chunks per head group, at most
+ROLE_SPLIT = 8
+# With nine warps one SM sub-partition holds three of them, so ptxas gives
+# each thread at most 168 registers at launch.  The warpgroups then re-divide
+# them (setmaxnreg): the softmax warps take REG_SOFTMAX, the producer / MMA
+# warps keep REG_ISSUE, the split warp keeps the launch count.  The shares
+# must fit the launch's registers (checked against ptxas's count).
+REG_LAUNCH, REG_SOFTMAX, REG_ISSUE = 168, 224, 96
+assert 128 * (REG_SOFTMAX + REG_ISSUE) + 32 * REG_LAUNCH <= 288 * REG_LAUNCH
+assert 128 * (REG_SOFTMAX + REG_ISSUE) <= 256 * REG_LAUNCH     # the 256-thread launch
 
 
 @dataclass
@@ -157,7 +180,25 @@ def match(comp) -> AttnPlan:
     return AttnPlan(B, H, S, D, scale, causal, ins[0], ins[1], ins[2], outs[0])
 
 
-def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: int = 256) -> str:
+def _split_values(b, x, y):
+    """K values ``x`` -> their tf32 lo parts (K minus K with its low 13 bits
+    cleared, exact); V values ``y`` -> rounded to the nearest tf32
+    (``cvt.rna``).  Returns the two register lists."""
+    lo = b.regs("f", len(x))
+    vr = b.regs("r", len(y))
+    for e in range(len(x)):
+        hb = b.reg("r")
+        b.ins(f"mov.b32 {hb}, {x[e]};")
+        b.ins(f"and.b32 {hb}, {hb}, 0xFFFFE000;")
+        hf = b.reg("f")
+        b.ins(f"mov.b32 {hf}, {hb};")
+        b.ins(f"sub.f32 {lo[e]}, {x[e]}, {hf};")
+        b.ins(f"cvt.rna.tf32.f32 {vr[e]}, {y[e]};")
+    return lo, vr
+
+
+def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: int = 256,
+                    split_groups: tuple | None = None) -> str:
     """The pre-pass entry ``entry(k, v, k_lo, v_r)``.  The tensor core reads
     an f32 operand as tf32 by dropping its low 13 bits, so the kernel loads
     K itself as the hi operand of 3xTF32 QK^T (the hardware forms
@@ -168,7 +209,14 @@ def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: 
     (32-byte accesses, PTX ISA 8.8) or 4 below 8.8; ``n_elems`` a multiple
     of the vector; returned without the module header.  With 32-byte
     vectors and 16 blocks per SM the full-size pass (2 GB) measured 0.332
-    ms against 0.368 with 16-byte vectors and 8 blocks per SM."""
+    ms against 0.368 with 16-byte vectors and 8 blocks per SM.
+
+    ``split_groups = (groups, chunks)``: the attention kernel splits every
+    head group but the first itself (``emit``, the split warp), and this
+    entry covers group 0 only (``n_elems`` = its elements).  Its thread 0
+    also prepares the kernel's split state in the module globals: the
+    ``k_lo`` / ``v_r`` addresses, the chunk counter at zero, and the
+    per-group chunks-done counts (group 0 complete, the others zero)."""
     vw = 8 if wide_vectors(version) else 4
     assert n_elems % vw == 0
     b = KernelBuilder(entry, target, version)
@@ -187,6 +235,37 @@ def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: 
     b.ins(f"mov.u32 {stride}, %nctaid.x;")
     b.ins(f"mul.lo.u32 {stride}, {stride}, {nt};")
     b.ins(f"mov.u32 {t}, %tid.x;")
+    if split_groups is not None:
+        ngroups, nchunks = split_groups
+        p0 = b.reg("p")
+        b.ins(f"or.b32 {g}, {g}, {t};")
+        b.ins(f"setp.ne.u32 {p0}, {g}, 0;")
+        skip = b.label("SPLIT_INIT_DONE")
+        b.ins(f"@{p0} bra {skip};")
+        ga = b.reg("rd")
+        for nm, glob in ((names[2], "emmy_split_lo"), (names[3], "emmy_split_vr")):
+            b.ins(f"mov.u64 {ga}, {glob};")
+            b.ins(f"st.global.u64 [{ga}], {ptrs[names.index(nm)]};")
+        zero, full = b.regs("r", 2)
+        b.ins(f"mov.u32 {zero}, 0;")
+        b.ins(f"mov.u32 {full}, {nchunks};")
+        b.ins(f"mov.u64 {ga}, emmy_split_next;")
+        b.ins(f"st.global.u32 [{ga}], {zero};")
+        b.ins(f"mov.u64 {ga}, emmy_split_done;")
+        b.ins(f"st.global.u32 [{ga}], {full};")
+        i, pi = b.reg("r"), b.reg("p")
+        loop, ldone = b.label("SPLIT_ZERO"), b.label("SPLIT_ZERO_END")
+        b.ins(f"mov.u32 {i}, 1;")
+        b.place(loop)
+        b.ins(f"setp.ge.u32 {pi}, {i}, {ngroups};")
+        b.ins(f"@{pi} bra {ldone};")
+        b.ins(f"add.s64 {ga}, {ga}, 4;")
+        b.ins(f"st.global.u32 [{ga}], {zero};")
+        b.ins(f"add.u32 {i}, {i}, 1;")
+        b.ins(f"bra {loop};")
+        b.place(ldone)
+        b.place(skip)
+        b.ins(f"mov.u32 {g}, %ctaid.x;")
     b.ins(f"mad.lo.u32 {g}, {g}, {nt}, {t};")
     top, done = b.label("PRE"), b.label("PRE_END")
     p = b.reg("p")
@@ -202,16 +281,7 @@ def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: 
     y = b.regs("f", vw)
     b.ins(f"ld.global.nc.L1::no_allocate.v{vw}.f32 {{{', '.join(x)}}}, [{a['k']}];")
     b.ins(f"ld.global.nc.L1::no_allocate.v{vw}.f32 {{{', '.join(y)}}}, [{a['v']}];")
-    vr = b.regs("r", vw)
-    lo = b.regs("f", vw)
-    for e in range(vw):
-        hb = b.reg("r")
-        b.ins(f"mov.b32 {hb}, {x[e]};")
-        b.ins(f"and.b32 {hb}, {hb}, 0xFFFFE000;")
-        hf = b.reg("f")
-        b.ins(f"mov.b32 {hf}, {hb};")
-        b.ins(f"sub.f32 {lo[e]}, {x[e]}, {hf};")
-        b.ins(f"cvt.rna.tf32.f32 {vr[e]}, {y[e]};")
+    lo, vr = _split_values(b, x, y)
     b.ins(f"st.global.v{vw}.f32 [{a['k_lo']}], {{{', '.join(lo)}}};")
     b.ins(f"st.global.v{vw}.b32 [{a['v_r']}], {{{', '.join(vr)}}};")
     b.ins(f"add.u32 {g}, {g}, {stride};")
@@ -292,6 +362,17 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     T = launch_block(comp) or 256
     if T != 256:
         raise NoMatch(f"the tcgen05 attention kernel needs 256 threads per block (meta.json has {T})")
+    G = head_group(B * H)
+    NG = B * H // G                    # head groups
+    # in-kernel split: chunks of a head group, each a whole number of the
+    # split warp's 32-lane vector rows
+    SVW = 8 if wide_vectors(comp.ptx_version) else 4
+    nvg = G * S * D // SVW             # vectors per head group
+    CH = max([c for c in range(1, SPLIT_CHUNKS + 1) if nvg % (32 * c) == 0] or [0])
+    inline = INLINE_SPLIT and not pair and NG > 1 and CH > 0
+    CHV = nvg // CH if inline else 0   # vectors per chunk
+    SUN = max(u for u in (1, 2, 4) if (CHV // 32) % u == 0) if inline else 1
+    TL = T + 32 if inline else T       # launch block: the split warp is warp 8
     DC = D // 32                       # 32-dim chunks
     nqt = -(-S // BQ)
     nqu = -(-nqt // CG)                # query units: tiles, or pairs of tiles
@@ -344,7 +425,15 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         b.module(f".global .align 8 .b8 emmy_gather_dst[{8 * gather}];")
         b.module(".global .align 4 .u32 emmy_gather_n;")
         b.module(".global .align 4 .u32 emmy_gather_row0;")
-    b.directive(f".maxntid {T}, 1, 1")
+    if inline:
+        # split state, prepared by the pre-pass entry before every launch
+        b.module(".global .align 8 .u64 emmy_split_lo;")
+        b.module(".global .align 8 .u64 emmy_split_vr;")
+        b.module(".global .align 4 .u32 emmy_split_next;")
+        b.module(f".global .align 4 .b8 emmy_split_done[{4 * NG}];")
+    b.directive(f".maxntid {TL}, 1, 1")
+    if inline:
+        b.directive(f".maxnreg {REG_LAUNCH}")
     if pair:
         # launching without the cluster of two fails at launch time
         b.directive(".reqnctapercluster 2, 1, 1")
@@ -382,6 +471,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     b.ins(f"add.u32 {slot}, {bars}, {QR + 72};")
     b.ins(f"add.u32 {abort}, {bars}, {QR + 76};")
     assert DRAIN2 + 8 <= BAR_BYTES
+
     tc = TC(b, abort, cta_group=CG)
 
     p = b.reg("p")
@@ -420,7 +510,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         b.ins("barrier.cluster.arrive.release.aligned;")
         b.ins("barrier.cluster.wait.acquire.aligned;")
     else:
-        b.ins(f"bar.sync 0, {T};")
+        b.ins("bar.sync 0;")
     b.ins("tcgen05.fence::after_thread_sync;")
     tmem = b.reg("r")
     b.ins(f"ld.shared.u32 {tmem}, [{slot}];")
@@ -455,8 +545,6 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
             b.ins(f"mad.lo.u32 {r}, {s}, 8, {reg_base};")
             b.ins(f"add.u32 {r}, {r}, {off};")
         return r
-
-    G = head_group(B * H)
 
     # the item sequence of this CTA (or pair): a precomputed table when the
     # launch has the grid the table was built for, else every ncta-th item
@@ -594,8 +682,31 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     roles = [b.label("SOFTMAX"), b.label("PRODUCER_K"), b.label("MMA_QK"), b.label("PRODUCER_V"),
              b.label("MMA_PV")]
     pr = b.reg("p")
-    b.ins(f"setp.lt.u32 {pr}, {warp}, 4;")
-    b.ins(f"@{pr} bra {roles[0]};")
+    if inline:
+        # warp 8 splits; a launch without it (the meta.json block of 256
+        # threads) has every warp split first, then take its role
+        pall, nth = b.reg("p"), b.reg("r")
+        SPLIT, DISPATCH = b.label("SPLIT"), b.label("DISPATCH")
+        b.ins(f"mov.u32 {nth}, %ntid.x;")
+        b.ins(f"setp.lt.u32 {pall}, {nth}, {TL};")
+        b.ins(f"@{pall} bra.uni {SPLIT};")
+        b.ins(f"setp.eq.u32 {pr}, {warp}, 8;")
+        b.ins(f"@{pr} bra.uni {SPLIT};")
+        b.place(DISPATCH)
+    if inline:
+        # register split per warpgroup, each right before its own roles so
+        # that a role's code is reached from one budget only: warps 0-3 take
+        # registers, warps 4-7 hand theirs back
+        wg1 = b.label("WG_ISSUE")
+        b.ins(f"setp.ge.u32 {pr}, {warp}, 4;")
+        b.ins(f"@{pr} bra {wg1};")
+        b.ins(f"setmaxnreg.inc.sync.aligned.u32 {REG_SOFTMAX};")
+        b.ins(f"bra.uni {roles[0]};")
+        b.place(wg1)
+        b.ins(f"setmaxnreg.dec.sync.aligned.u32 {REG_ISSUE};")
+    else:
+        b.ins(f"setp.lt.u32 {pr}, {warp}, 4;")
+        b.ins(f"@{pr} bra {roles[0]};")
     b.ins(f"setp.eq.u32 {pr}, {warp}, 4;")
     b.ins(f"@{pr} bra {roles[1]};")
     b.ins(f"setp.eq.u32 {pr}, {warp}, 5;")
@@ -603,6 +714,131 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     b.ins(f"setp.eq.u32 {pr}, {warp}, 6;")
     b.ins(f"@{pr} bra {roles[3]};")
     b.ins(f"bra.uni {roles[4]};")              # warp 7
+
+    if inline:
+        # ---- split warp: K's lo part and the rounded V of groups 1.. ---------
+        # Chunk c (groups 1.. in order, CH chunks each) is taken from the
+        # shared counter, so the resident warps share the work whatever the
+        # grid; a chunk's completion is released on its group's counter,
+        # which the producers acquire before their TMA loads of that group.
+        b.place(SPLIT)
+        lo_b, vr_b, ga = b.regs("rd", 3)
+        b.ins(f"mov.u64 {ga}, emmy_split_lo;")
+        b.ins(f"ld.global.u64 {lo_b}, [{ga}];")
+        b.ins(f"mov.u64 {ga}, emmy_split_vr;")
+        b.ins(f"ld.global.u64 {vr_b}, [{ga}];")
+        # the pre-pass entry records the scratch addresses; without it there
+        # is nothing to write to: report and leave (the producers' bounded
+        # waits then end the kernel)
+        pz, pz2 = b.regs("p", 2)
+        have = b.label("SPLIT_HAVE_SCRATCH")
+        b.ins(f"setp.eq.u64 {pz}, {lo_b}, 0;")
+        b.ins(f"setp.eq.u64 {pz2}, {vr_b}, 0;")
+        b.ins(f"or.pred {pz}, {pz}, {pz2};")
+        b.ins(f"@!{pz} bra.uni {have};")
+        tc.raise_abort(STATUS_NO_PREPASS)
+        b.ins(f"bra.uni {END};")
+        b.place(have)
+        nxt, dn = b.regs("rd", 2)
+        b.ins(f"mov.u64 {nxt}, emmy_split_next;")
+        b.ins(f"mov.u64 {dn}, emmy_split_done;")
+        pl0 = b.reg("p")
+        b.ins(f"setp.eq.u32 {pl0}, {lane}, 0;")
+        loff = b.reg("rd")                 # this lane's first vector in a chunk
+        b.ins(f"mul.wide.u32 {loff}, {lane}, {SVW * 4};")
+        c = b.reg("r")
+        stop = b.label("SPLIT_NEXT")
+        send = b.label("SPLIT_END")
+        b.place(stop)
+        b.ins(f"@{pl0} atom.global.add.u32 {c}, [{nxt}], 1;")
+        b.ins(f"shfl.sync.idx.b32 {c}, {c}, 0, 0x1f, 0xffffffff;")
+        pc = b.reg("p")
+        b.ins(f"setp.ge.u32 {pc}, {c}, {(NG - 1) * CH};")
+        b.ins(f"@{pc} bra.uni {send};")
+        cg = b.reg("r")                    # chunk index counting group 0's
+        b.ins(f"add.u32 {cg}, {c}, {CH};")
+        grp = b.reg("r")
+        b.ins(f"div.u32 {grp}, {cg}, {CH};")
+        off = b.reg("rd")
+        b.ins(f"mul.wide.u32 {off}, {cg}, {CHV * SVW * 4};")
+        b.ins(f"add.s64 {off}, {off}, {loff};")
+        pk, pv, plo, pvr = b.regs("rd", 4)
+        for dst, base_ in ((pk, ptrs[plan.k]), (pv, ptrs[plan.v]), (plo, lo_b), (pvr, vr_b)):
+            b.ins(f"add.s64 {dst}, {base_}, {off};")
+        step = 32 * SVW * 4                # bytes between a lane's vectors
+        trips = b.reg("r")
+        b.ins(f"mov.u32 {trips}, {CHV // 32 // SUN};")
+        ltop = b.label("SPLIT_VEC")
+        b.place(ltop)
+        xs, ys = [], []
+        for u in range(SUN):
+            x = b.regs("f", SVW)
+            y = b.regs("f", SVW)
+            b.ins(f"ld.global.nc.L1::no_allocate.v{SVW}.f32 {{{', '.join(x)}}}, "
+                  f"[{pk}+{u * step}];")
+            b.ins(f"ld.global.nc.L1::no_allocate.v{SVW}.f32 {{{', '.join(y)}}}, "
+                  f"[{pv}+{u * step}];")
+            xs.append(x)
+            ys.append(y)
+        for u in range(SUN):
+            lo, vr = _split_values(b, xs[u], ys[u])
+            b.ins(f"st.global.v{SVW}.f32 [{plo}+{u * step}], {{{', '.join(lo)}}};")
+            b.ins(f"st.global.v{SVW}.b32 [{pvr}+{u * step}], {{{', '.join(vr)}}};")
+        for r_ in (pk, pv, plo, pvr):
+            b.ins(f"add.s64 {r_}, {r_}, {SUN * step};")
+        pt_ = b.reg("p")
+        b.ins(f"sub.u32 {trips}, {trips}, 1;")
+        b.ins(f"setp.ne.u32 {pt_}, {trips}, 0;")
+        b.ins(f"@{pt_} bra.uni {ltop};")
+        # this warp's writes of the chunk, then its release on the group
+        b.ins("fence.proxy.async.global;")
+        b.ins("bar.warp.sync 0xffffffff;")
+        ga4 = b.reg("rd")
+        b.ins(f"mul.wide.u32 {ga4}, {grp}, 4;")
+        b.ins(f"add.s64 {ga4}, {ga4}, {dn};")
+        b.ins(f"@{pl0} red.release.gpu.global.add.u32 [{ga4}], 1;")
+        b.ins(f"bra.uni {stop};")
+        b.place(send)
+        b.ins(f"@{pall} bra.uni {DISPATCH};")
+        b.ins(f"bra.uni {END};")
+
+    def wait_split(w):
+        """The producers' wait (before the TMA loads of item w's K lo or
+        rounded V): every chunk of w's head group is done.  Bounded like
+        every wait; a timeout sets the status word and leaves."""
+        if not inline:
+            return
+        g_, a_, o_ = b.reg("r"), b.reg("rd"), b.reg("rd")
+        b.ins(f"div.u32 {g_}, {w}, {G * nqu};")
+        b.ins(f"mov.u64 {a_}, emmy_split_done;")
+        b.ins(f"mul.wide.u32 {o_}, {g_}, 4;")
+        b.ins(f"add.s64 {a_}, {a_}, {o_};")
+        v_, fl = b.regs("r", 2)
+        pw, pf = b.regs("p", 2)
+        t0, t1 = b.regs("rd", 2)
+        ok, top = b.label("SPLIT_READY"), b.label("SPLIT_WAIT")
+        b.ins(f"ld.acquire.gpu.global.u32 {v_}, [{a_}];")
+        b.ins(f"setp.ge.u32 {pw}, {v_}, {CH};")
+        b.ins(f"@{pw} bra {ok};")
+        b.ins(f"mov.u64 {t0}, %globaltimer;")
+        b.place(top)
+        b.ins("nanosleep.u32 256;")
+        b.ins(f"ld.acquire.gpu.global.u32 {v_}, [{a_}];")
+        b.ins(f"setp.ge.u32 {pw}, {v_}, {CH};")
+        b.ins(f"@{pw} bra {ok};")
+        b.ins(f"ld.volatile.shared.u32 {fl}, [{abort}];")
+        b.ins(f"setp.ne.u32 {pf}, {fl}, 0;")
+        b.ins(f"@{pf} bra {END};")
+        b.ins(f"mov.u64 {t1}, %globaltimer;")
+        b.ins(f"sub.u64 {t1}, {t1}, {t0};")
+        b.ins(f"setp.lt.u64 {pf}, {t1}, {tc.limit_ns};")
+        b.ins(f"@{pf} bra {top};")
+        tc.raise_abort(STATUS_TIMEOUT + ROLE_SPLIT)
+        b.ins(f"bra {END};")
+        b.place(ok)
+        # the group's generic-proxy writes, acquired above, before this
+        # thread's async-proxy (TMA) reads of them
+        b.ins("fence.proxy.async.global;")
 
     # ---- producers: K (hi and lo) on warp 4, V on warp 6 -----------------------
     # Separate threads, so a K slot is refilled as soon as its QK^T chunk is
@@ -640,6 +876,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     def prod_k_item(w, _k):
         bh, qu = item_coords(w)
         nkv = n_kv(qu)
+        wait_split(w)
 
         def tile(j):
             k0 = b.reg("r")
@@ -677,6 +914,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     def prod_v_item(w, _k):
         bh, qu = item_coords(w)
         nkv = n_kv(qu)
+        wait_split(w)
         x0 = b.reg("r")                   # this CTA's first head dim
         b.ins(f"mul.lo.u32 {x0}, {rank}, {32 * VDC};")
 
@@ -1302,7 +1540,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     tc.wait(f"{bars}+{DRAIN2}", 0, pdl, ROLE_MMA, peer=False)
     b.place(pdl)
     b.ins("bar.warp.sync 0xffffffff;")
-    b.ins(f"bar.sync 0, {T};")
+    b.ins("bar.sync 0;")
     fin = b.label("FIN")
     b.ins(f"setp.ne.u32 {p}, {warp}, 5;")
     b.ins(f"@{p} bra {fin};")
@@ -1334,8 +1572,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     tc.tmem_dealloc(tmem, TMEM_COLS)
     b.place(fin)
 
+    pre_elems = G * S * D if inline else B * H * S * D
     ptx = b.render() + "\n" + emit_kv_prepass(comp.target, comp.ptx_version, split_entry,
-                                              B * H * S * D)
+                                              pre_elems,
+                                              split_groups=(NG, CH) if inline else None)
 
     pairs = B * H * (S * (S + 1) // 2 if plan.causal else S * S)
     kv_tiles = 0                      # (128-query tile, 128-key tile) products issued
@@ -1352,14 +1592,22 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     sidecar = {
         "category": "attention",
         "grid": [CG * min(items, 148 // CG), 1, 1],
-        "block": [T, 1, 1],
+        "block": [TL, 1, 1],
         "shared_bytes": SMEM,
         "cluster": [CG, 1, 1],
         "scratch": [{"name": "k_lo", "bytes": kbytes},
                     {"name": "v_r", "bytes": kbytes}],
         "prelaunch": [split_launch(split_entry, [plan.k, plan.v, "@k_lo", "@v_r"],
-                                   B * H * S * D, max_blocks=148 * 16,
+                                   pre_elems, max_blocks=148 * 16,
                                    vec=8 if wide_vectors(comp.ptx_version) else 4)],
+        "inline_split": {"groups": NG, "chunks_per_group": CH, "warp": 8} if inline else None,
+        # setmaxnreg shares: registers per thread at launch, and the total the
+        # warpgroups hold after the split, for the tuned block and the
+        # meta.json one (the runtime refuses a build with fewer at launch)
+        "register_split": {"launch": REG_LAUNCH, "softmax": REG_SOFTMAX, "issue": REG_ISSUE,
+                           "registers_by_block": {
+                               str(TL): 128 * (REG_SOFTMAX + REG_ISSUE) + 32 * REG_LAUNCH,
+                               str(T): 128 * (REG_SOFTMAX + REG_ISSUE)}} if inline else None,
         "tensormaps": [tmap("tmap_Khi", plan.k, "128B"),     # K itself: hi = K, low bits dropped
                        tmap("tmap_Klo", "@k_lo", "128B"),
                        tmap("tmap_V", "@v_r", "128B_atom32B")],

@@ -27,6 +27,7 @@ WAIT_LIMIT_NS = 2_000_000_000      # 2 s per wait before the kernel gives up
 
 # status codes written to emmy_status
 STATUS_TIMEOUT = 0x100             # + role id
+STATUS_NO_PREPASS = 0x200          # a kernel's pre-pass entry did not run before it
 
 SWIZZLE_MODE = {"none": 0, "128B_base32B": 1, "128B": 2, "64B": 4, "32B": 6}
 

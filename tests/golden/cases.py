@@ -28,6 +28,11 @@ PARITY = {
     "attention_2x1x40x64": ("attention", dict(batch=2, heads=1, seq=40, head_dim=64)),
     "attention_noncausal_1x2x48x64": ("attention", dict(batch=1, heads=2, seq=48, head_dim=64,
                                                         causal=False)),
+    # several head groups: the kernel splits groups 1.. itself (its split warp)
+    "attention_2x8x256x128": ("attention", dict(batch=2, heads=8, seq=256, head_dim=128)),
+    "attention_3x5x256x64": ("attention", dict(batch=3, heads=5, seq=256, head_dim=64)),
+    "attention_noncausal_2x6x192x64": ("attention", dict(batch=2, heads=6, seq=192, head_dim=64,
+                                                         causal=False)),
     "pointwise_zoo_16x64": ("pointwise_zoo", dict(rows=16, cols=64)),
     "pointwise_mixed_16x64": ("pointwise_mixed", dict(rows=16, cols=64)),
     "bit_ops_16x64": ("bit_ops", dict(rows=16, cols=64)),

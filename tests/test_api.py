@@ -148,5 +148,9 @@ def test_every_config_has_an_sm100a_lowering(name, tmp_path):
     ptx = comp.compile()
     side = comp.sidecar()
     assert ".target sm_100a" in ptx
-    assert side["block"][0] == p.block[0], "the kernel keeps the meta.json block size"
+    # the kernel keeps the meta.json block size; attention with several head
+    # groups adds its split warp to the tuned launch and still runs (split
+    # first, then compute) on the meta.json block
+    extra = 32 if side.get("inline_split") else 0
+    assert side["block"][0] == p.block[0] + extra, "the kernel keeps the meta.json block size"
     assert side["arg_order"] == p.inputs + p.outputs

@@ -184,3 +184,52 @@ def test_row_gather_variant_stores_to_every_destination(tmp_path, name, kw):
     report = _build.ptxas_check(ptx)
     assert "0 bytes spill stores" in report, report
 
+
+
+@pytest.mark.parametrize("kw,groups,chunks", [
+    (dict(batch=2, heads=8, seq=256, head_dim=128), 2, 128),
+    (dict(batch=3, heads=5, seq=256, head_dim=64), 3, 80),
+    (dict(batch=8, heads=32, seq=4096, head_dim=128), 32, 128)])
+def test_attention_splits_head_groups_in_the_kernel(tmp_path, kw, groups, chunks):
+    """With several head groups the pre-pass covers group 0 and prepares the
+    split state; a ninth warp takes chunks of the later groups from a shared
+    counter and releases each on its group's count, which the producers
+    acquire (bounded) before their TMA loads.  The warpgroups re-divide the
+    168 registers per thread of the 288-thread launch with setmaxnreg, and the
+    shares fit both the tuned block and the meta.json block of 256."""
+    from emmy_ptx import workloads
+    from emmy_ptx.sm100 import attention
+    p = workloads.attention(causal=True, **kw)
+    comp = Compiler(p.write(tmp_path), target="sm_100a", ptx_version="8.8")
+    ptx, side = attention.emit(comp, attention.match(comp))
+    assert side["inline_split"] == {"groups": groups, "chunks_per_group": chunks, "warp": 8}
+    assert side["block"] == [288, 1, 1]
+    rs = side["register_split"]
+    assert rs["launch"] == 168
+    for threads, need in rs["registers_by_block"].items():
+        assert need <= int(threads) * rs["launch"]
+    main, pre = ptx.split(".visible .entry k_attention_causal_ksplit(")
+    assert ".maxntid 288, 1, 1" in main and ".maxnreg 168" in main
+    assert main.count("setmaxnreg.inc.sync.aligned.u32 224;") == 1
+    assert main.count("setmaxnreg.dec.sync.aligned.u32 96;") == 1
+    assert main.count("atom.global.add.u32") == 1
+    assert main.count("red.release.gpu.global.add.u32") == 1
+    assert main.count("ld.acquire.gpu.global.u32") == 4          # two per producer
+    assert "nanosleep" in main and "fence.proxy.async.global;" in main
+    assert "bar.sync 0, 256" not in main                        # CTA-wide barriers only
+    # the pre-pass covers head group 0: (batch*heads / groups) heads of K
+    b, h, s, d = kw["batch"], kw["heads"], kw["seq"], kw["head_dim"]
+    assert f"setp.ge.u32 %p3, %r1, {b * h // groups * s * d // 8};" in pre
+    assert "emmy_split_done" in pre and "emmy_split_next" in pre
+    report = _build.ptxas_check(ptx)
+    assert "0 bytes spill stores" in report and "Used 168 registers" in report, report
+
+
+def test_attention_with_one_head_group_keeps_the_whole_pre_pass(tmp_path):
+    from emmy_ptx import workloads
+    from emmy_ptx.sm100 import attention
+    p = workloads.attention(batch=1, heads=2, seq=256, head_dim=128, causal=True)
+    comp = Compiler(p.write(tmp_path), target="sm_100a", ptx_version="8.8")
+    ptx, side = attention.emit(comp, attention.match(comp))
+    assert side["inline_split"] is None and side["register_split"] is None
+    assert side["block"] == [256, 1, 1] and "setmaxnreg" not in ptx
