@@ -24,6 +24,8 @@ PARITY = {
     "rowsum_i32_7x68": ("rowsum_i32", dict(rows=7, cols=68)),
     "matmul_128x128x64": ("matmul", dict(m=128, n=128, k=64)),
     "matmul_256x384x128": ("matmul", dict(m=256, n=384, k=128)),
+    # four K groups of 256: the kernel's warps 2-3 split groups 1-3 themselves
+    "matmul_256x256x1024": ("matmul", dict(m=256, n=256, k=1024)),
     "attention_1x2x64x128": ("attention", dict(batch=1, heads=2, seq=64, head_dim=128)),
     "attention_2x1x40x64": ("attention", dict(batch=2, heads=1, seq=40, head_dim=64)),
     "attention_noncausal_1x2x48x64": ("attention", dict(batch=1, heads=2, seq=48, head_dim=64,
