@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import ctypes
 import json
+import re
 import threading
 from pathlib import Path
 
@@ -178,6 +179,23 @@ def _stream_handle(stream) -> int:
     return int(h)
 
 
+_VEC_ACCESS = re.compile(r"\b(?:ld|st)\.global[.\w:]*?\.v(\d)\.[bfsu](\d+)\b")
+
+
+def required_alignment(ptx: str) -> int:
+    """The address alignment a module's global accesses need: the largest
+    vector access (``ld/st.global...vN.<type>``), 16 bytes if it moves data
+    with bulk copies (TMA, ``cp.async.bulk``), else 0.  A pointer argument
+    off that alignment would fault the kernel, so ``Kernel.bind`` refuses
+    it."""
+    need = 0
+    for n, bits in _VEC_ACCESS.findall(ptx):
+        need = max(need, int(n) * int(bits) // 8)
+    if "cp.async.bulk" in ptx:
+        need = max(need, 16)
+    return need
+
+
 def _ptr(x) -> int:
     if isinstance(x, int):
         return x
@@ -325,6 +343,7 @@ class Kernel:
         self.module = Module(ptx)
         self.function = self.module.function(entry)
         self._check_register_split()
+        self.alignment = required_alignment(ptx)
         self._tmap_cache: dict = {}
         self.launches = 0
         # scratch buffers the kernel needs beyond its arguments (sidecar
@@ -438,6 +457,10 @@ class Kernel:
             else:
                 self._validate(a, v)
                 p = _ptr(v)
+                if self.alignment and p % self.alignment:
+                    raise EmmyRuntimeError(
+                        f"argument {a['name']!r}: address {p:#x} is not {self.alignment}-byte "
+                        f"aligned, as {self.entry}'s vector accesses need")
                 ptrs[a["name"]] = p
                 values.append(ctypes.c_uint64(p))
         ptrs.update(self._scratch_ptrs())

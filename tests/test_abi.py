@@ -57,3 +57,18 @@ def test_runtime_refuses_to_run_without_a_device():
         pytest.skip("a GPU is present")
     with pytest.raises(rt.EmmyRuntimeError):
         rt.init(0)
+
+
+def test_required_alignment_follows_the_widest_vector_access():
+    """Kernel.bind refuses a pointer off the alignment the module's widest
+    global vector access (or a bulk copy) needs, instead of launching a
+    kernel that would fault on it."""
+    assert rt.required_alignment("ld.global.f32 %f1, [%rd1];") == 0
+    assert rt.required_alignment("ld.global.nc.v4.f32 {%f1,%f2,%f3,%f4}, [%rd1];") == 16
+    assert rt.required_alignment("ld.global.nc.v2.f64 {%fd1,%fd2}, [%rd1];") == 16
+    assert rt.required_alignment(
+        "ld.global.nc.L1::no_allocate.v8.f32 {%f1}, [%rd1];\nst.global.v4.f32 [%rd2], {%f1};") == 32
+    assert rt.required_alignment("st.global.v8.b32 [%rd1], {%r1};") == 32
+    assert rt.required_alignment(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%r1], [%rd1], 16, [%r2];"
+    ) == 16

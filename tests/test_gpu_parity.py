@@ -142,3 +142,23 @@ def test_two_binds_of_a_tensor_map_kernel_keep_their_own_buffers(cuda):
         ok, msg = check_close("matmul", f"C of bind {i}", dev["C"].cpu().numpy(), want, host)
         assert ok, msg
     assert kern.status() == 0
+
+
+@pytest.mark.gpu
+def test_misaligned_argument_is_refused_before_launch(cuda):
+    """A pointer 4 bytes off the 32-byte vectors of the pointwise kernel is
+    refused at bind time; nothing is launched."""
+    import torch
+    from emmy_ptx import workloads
+    from emmy_ptx.runtime import EmmyRuntimeError, Kernel
+    p = workloads.build("pointwise_f32", rows=64, cols=256)
+    with tempfile.TemporaryDirectory() as td:
+        kern = Kernel.from_ir(p.write(td))
+    assert kern.alignment >= 16
+    n = 64 * 256
+    x = torch.zeros(n + 8, device=cuda)
+    y = torch.zeros(n, device=cuda)
+    out = torch.zeros(n, device=cuda)
+    with pytest.raises(EmmyRuntimeError, match="aligned"):
+        kern.bind({"x": x[1:n + 1], "y": y, "out": out})
+    assert kern.launches == 0
