@@ -30,12 +30,10 @@ from .common import (NoMatch, Program, Sym, declare_params, emit_program, flat_a
                      launch_block, literal_sym, nbytes, const_value)
 from .ops import Ops, dtype_name, is_float
 from .pointwise import result_dtype
-from .ptx import KernelBuilder, MEM_TYPE, wide_vectors
+from .ptx import KernelBuilder, MEM_TYPE
 from .rows import _RED_OPS, _IDENT, _INT_IDENT, _combine
 
 ROWS_IN_FLIGHT = 4
-# 32-byte lane vectors (.v4 of 8-byte / .v8 of 4-byte values, PTX ISA 8.8)
-WIDE = False
 
 
 @dataclass
@@ -186,10 +184,7 @@ def emit(comp, plan: ColPlan):
     NW = T // 32
     dt = plan.dtype
     esz = nbytes(dt)
-    vb = 32 if (WIDE and wide_vectors(comp.ptx_version)) else 16   # bytes per lane vector
-    VL = vb // esz if plan.cols % (32 * (vb // esz)) == 0 else 1
-    if VL == 1 and vb == 32 and plan.cols % (32 * (16 // esz)) == 0:
-        VL = 16 // esz
+    VL = 16 // esz if plan.cols % (32 * (16 // esz)) == 0 else 1
     CW = 32 * VL
     strips = -(-plan.cols // CW)
     meta_grid = 1
