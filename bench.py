@@ -200,13 +200,14 @@ def time_kernel(bound, reps, warmup, stream):
 # ----------------------------------------------------------------------------
 # end to end through the host-buffer C-ABI path
 # ----------------------------------------------------------------------------
-def link_probe(device, h2d_bytes, d2h_bytes, barrier, max_over_ranks, reps=3):
+def link_probe(device, h2d_bytes, d2h_bytes, barrier, max_over_ranks, reps=3, chunks=16):
     """The ceiling of the end-to-end step: the same volume moved the same way
     with no kernels -- every rank copies its step's inputs in and outputs out
-    (pinned host buffers, one stream per direction, one cudaMemcpyAsync per
-    direction, both in flight at once), all ranks starting together after a
-    barrier, timed with CUDA events, max over ranks; best of ``reps`` after
-    a warm-up.  Returns (ms, this rank's own ms)."""
+    (pinned host buffers, one stream per direction, both in flight at once,
+    each direction in ``chunks`` copies as the pipeline makes them), all
+    ranks starting together after a barrier, timed with CUDA events, max
+    over ranks; best of ``reps`` after a warm-up.  Returns (ms, this rank's
+    own ms)."""
     import torch
     h_in = torch.empty(h2d_bytes // 4, dtype=torch.float32).pin_memory()
     h_out = torch.empty(d2h_bytes // 4, dtype=torch.float32).pin_memory()
@@ -223,9 +224,11 @@ def link_probe(device, h2d_bytes, d2h_bytes, barrier, max_over_ranks, reps=3):
         s_in.wait_stream(cur)
         s_out.wait_stream(cur)
         with torch.cuda.stream(s_in):
-            d_in.copy_(h_in, non_blocking=True)
+            for a, b_ in zip(d_in.chunk(chunks), h_in.chunk(chunks)):
+                a.copy_(b_, non_blocking=True)
         with torch.cuda.stream(s_out):
-            h_out.copy_(d_out, non_blocking=True)
+            for a, b_ in zip(h_out.chunk(chunks), d_out.chunk(chunks)):
+                a.copy_(b_, non_blocking=True)
         cur.wait_stream(s_in)
         cur.wait_stream(s_out)
         e.record(cur)
@@ -683,7 +686,7 @@ def run_b200(args):
     e2e_value = world * e2e["bytes"] / et / 1e6
     # the same copies with no kernels, all ranks at once: the step's ceiling
     link_ms, link_mine = link_probe(device, e2e["h2d"] // 4 * 4, e2e["d2h"] // 4 * 4,
-                                    barrier, max_over_ranks)
+                                    barrier, max_over_ranks, chunks=2 * chunks)
     link_total = world * (e2e["h2d"] + e2e["d2h"]) / link_ms / 1e6
     links = [round((e2e["h2d"] + e2e["d2h"]) / link_mine / 1e6, 1)]
     if world > 1:
@@ -724,8 +727,9 @@ def run_b200(args):
                 "link_both_ways_gbs": round(link_total, 1),
                 "link_ms_per_step": round(link_ms, 3),
                 "link_per_rank_gbs": links,
-                "link": "the step's copies alone (no kernels), both directions at once, "
-                        "all ranks together, max over ranks",
+                "link": f"the step's copies alone (no kernels), both directions at once, "
+                        f"{2 * chunks} copies per direction as the pipeline makes them, "
+                        f"all ranks together, max over ranks",
                 "frac_of_link": round(pcie_total / link_total, 3),
                 "path": f"emmy_ptx.pipeline.ChunkedHostRunner: pinned host -> ert_memcpy_htod "
                         f"-> launch -> ert_memcpy_dtoh, {e2e['chunks']} row blocks per rank "
