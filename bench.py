@@ -224,11 +224,11 @@ def link_probe(device, h2d_bytes, d2h_bytes, barrier, max_over_ranks, reps=3, ch
         s_in.wait_stream(cur)
         s_out.wait_stream(cur)
         with torch.cuda.stream(s_in):
-            for a, b_ in zip(d_in.chunk(chunks), h_in.chunk(chunks)):
-                a.copy_(b_, non_blocking=True)
+            for dst, src in zip(d_in.chunk(chunks), h_in.chunk(chunks)):
+                dst.copy_(src, non_blocking=True)
         with torch.cuda.stream(s_out):
-            for a, b_ in zip(h_out.chunk(chunks), d_out.chunk(chunks)):
-                a.copy_(b_, non_blocking=True)
+            for dst, src in zip(h_out.chunk(chunks), d_out.chunk(chunks)):
+                dst.copy_(src, non_blocking=True)
         cur.wait_stream(s_in)
         cur.wait_stream(s_out)
         e.record(cur)
