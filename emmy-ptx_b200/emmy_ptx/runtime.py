@@ -444,7 +444,8 @@ class Kernel:
         scalar value) once; the returned launch object re-launches with no
         per-call argument marshalling.  Auxiliary launches the sidecar lists
         under ``prelaunch`` (e.g. a pre-pass over an input into scratch
-        memory) run first, on the same stream."""
+        memory) run first, and those under ``postlaunch`` (e.g. the sum of a
+        split-K kernel's partial tiles) after it, on the same stream."""
         s = _stream_handle(stream)
         values = []
         ptrs = {}
@@ -466,17 +467,22 @@ class Kernel:
         ptrs.update(self._scratch_ptrs())
         self._prepare_tensormaps(ptrs, s)
         main = BoundLaunch(self, values, self.geometry(geometry), s, tmap_ptrs=ptrs)
-        pre = []
-        for aux in self.sidecar.get("prelaunch") or []:
-            fn = self.module.function(aux["entry"])
-            vals = [ctypes.c_uint64(ptrs[a]) for a in aux["args"]]
-            g = ErtGeom()
-            g.grid[:] = (list(aux["grid"]) + [1, 1, 1])[:3]
-            g.block[:] = (list(aux["block"]) + [1, 1, 1])[:3]
-            g.cluster[:] = (1, 1, 1)
-            g.shared_bytes = int(aux.get("shared_bytes", 0))
-            pre.append(BoundLaunch(self, vals, g, s, function=fn))
-        return main if not pre else LaunchSequence(pre + [main])
+        def aux_launches(key):
+            out = []
+            for aux in self.sidecar.get(key) or []:
+                fn = self.module.function(aux["entry"])
+                vals = [ctypes.c_uint64(ptrs[a]) for a in aux["args"]]
+                g = ErtGeom()
+                g.grid[:] = (list(aux["grid"]) + [1, 1, 1])[:3]
+                g.block[:] = (list(aux["block"]) + [1, 1, 1])[:3]
+                g.cluster[:] = (1, 1, 1)
+                g.shared_bytes = int(aux.get("shared_bytes", 0))
+                out.append(BoundLaunch(self, vals, g, s, function=fn))
+            return out
+        # prelaunch entries (pre-passes) before the kernel, postlaunch
+        # entries (the split-K reduction) after it, all on the same stream
+        pre, post = aux_launches("prelaunch"), aux_launches("postlaunch")
+        return main if not (pre or post) else LaunchSequence(pre + [main] + post)
 
     def launch(self, buffers: dict, *, stream=None, geometry="tuned"):
         """Launch with ``buffers`` mapping every argument name to a device

@@ -47,8 +47,8 @@ from .. import ir as I
 from .common import NoMatch, declare_params, launch_block
 from .ops import dtype_name
 from .ptx import KernelBuilder
-from .tc import (TC, emit_tf32_split, idesc_f8, idesc_f16, idesc_tf32, smem_desc_hi,
-                 split_launch)
+from .tc import (STATUS_NO_PREPASS, TC, emit_tf32_split, idesc_f8, idesc_f16, idesc_tf32,
+                 smem_desc_hi, split_launch)
 
 BM = 128
 BK = 16
@@ -57,6 +57,34 @@ PAIR_STAGES = 6          # a pair's stages are smaller (half of each B tile per 
 GROUP_M = 8
 PAIR = True              # CTA pairs (tcgen05 cta_group::2) where the shapes allow
 ROLE_PRODUCER, ROLE_MMA, ROLE_EPILOGUE, ROLE_TEARDOWN = 1, 2, 4, 5
+SPLIT_K_CHOICES = (1, 2)      # K slices per output tile (f32), see choose_split_k
+SPLIT_K_MIN_K = 1024          # at least this much K per slice
+SPLIT_K_MIN_GAIN = 0.05       # wave efficiency a split must add to be used
+
+
+def wave_efficiency(units: int, slots: int) -> float:
+    """Busy fraction of ``slots`` concurrent workers over ``units`` equal
+    work units (the last wave partly idle)."""
+    return units / (-(-units // slots) * slots)
+
+
+def choose_split_k(ntiles: int, slots: int, k: int, bk: int) -> int:
+    """K slices per tile for an f32 matmul whose tiles fill the GPU badly:
+    a 2048 x 8192 shard has 256 pair tiles for 74 CTA pairs (3.46 waves,
+    0.865 busy); cut in two along K it is 512 units in 6.92 waves (0.988),
+    and measured 1.10 against 1.16 ms.  A slice writes its partial tile to
+    scratch and a reduce entry sums the slices, so a split must gain
+    SPLIT_K_MIN_GAIN of wave efficiency.  Four slices of a 1024-row shard
+    (0.865 -> 0.988 busy) measured no faster (0.607 against 0.609 ms): the
+    partial tiles and their sum cost what the fuller waves save."""
+    best, best_eff = 1, wave_efficiency(ntiles, slots)
+    for s in SPLIT_K_CHOICES[1:]:
+        if k % (s * bk) or k // s < SPLIT_K_MIN_K:
+            continue
+        e = wave_efficiency(ntiles * s, slots)
+        if e > best_eff + SPLIT_K_MIN_GAIN:
+            best, best_eff = s, e
+    return best
 
 
 @dataclass
@@ -136,7 +164,77 @@ def pair_ok(comp, plan: MatmulPlan) -> bool:
     return PAIR and plan.m > BM and plan.n > 128 and g[0] % 2 == 0
 
 
-def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None):
+def _emit_record_part(target: str, version: str, entry: str) -> str:
+    """``entry(part)``: one thread stores the partial tiles' scratch address
+    into the module global ``emmy_part`` (a prelaunch of split-K kernels).
+    Returned without the module header."""
+    b = KernelBuilder(entry, target, version)
+    b.directive(".maxntid 32, 1, 1")
+    pp = b.param("part", ".u64")
+    r, g = b.regs("rd", 2)
+    t = b.reg("r")
+    p = b.reg("p")
+    b.ins(f"ld.param.u64 {r}, [{pp}];")
+    b.ins(f"cvta.to.global.u64 {r}, {r};")
+    b.ins(f"mov.u32 {t}, %tid.x;")
+    b.ins(f"setp.ne.u32 {p}, {t}, 0;")
+    done = b.label("PART_DONE")
+    b.ins(f"@{p} bra {done};")
+    b.ins(f"mov.u64 {g}, emmy_part;")
+    b.ins(f"st.global.u64 [{g}], {r};")
+    b.place(done)
+    return b.render(header=False)
+
+
+def _emit_reduce(target: str, version: str, entry: str, n: int, slices: int,
+                 block: int = 256) -> str:
+    """``entry(part, c)``: ``c[i] = part[0][i] + part[1][i] + ...`` over the
+    ``slices`` partial results of ``n`` values each, added in slice order
+    (deterministic).  Grid-stride over 16-byte vectors; returned without the
+    module header."""
+    assert n % 4 == 0
+    b = KernelBuilder(entry, target, version)
+    b.directive(f".maxntid {block}, 1, 1")
+    pp, pc = b.param("part", ".u64"), b.param("c", ".u64")
+    part, c = b.regs("rd", 2)
+    for r, p_ in ((part, pp), (c, pc)):
+        b.ins(f"ld.param.u64 {r}, [{p_}];")
+        b.ins(f"cvta.to.global.u64 {r}, {r};")
+    g, stride, t, nt = b.regs("r", 4)
+    b.ins(f"mov.u32 {g}, %ctaid.x;")
+    b.ins(f"mov.u32 {nt}, %ntid.x;")
+    b.ins(f"mov.u32 {stride}, %nctaid.x;")
+    b.ins(f"mul.lo.u32 {stride}, {stride}, {nt};")
+    b.ins(f"mov.u32 {t}, %tid.x;")
+    b.ins(f"mad.lo.u32 {g}, {g}, {nt}, {t};")
+    top, done = b.label("RED"), b.label("RED_END")
+    p = b.reg("p")
+    b.place(top)
+    b.ins(f"setp.ge.u32 {p}, {g}, {n // 4};")
+    b.ins(f"@{p} bra {done};")
+    off = b.reg("rd")
+    b.ins(f"mul.wide.u32 {off}, {g}, 16;")
+    src = b.reg("rd")
+    b.ins(f"add.s64 {src}, {part}, {off};")
+    vals = []
+    for sl in range(slices):
+        v = b.regs("f", 4)
+        b.ins(f"ld.global.nc.L1::no_allocate.v4.f32 {{{', '.join(v)}}}, [{src}+{sl * n * 4}];")
+        vals.append(v)
+    acc = vals[0]
+    for v in vals[1:]:
+        for e in range(4):
+            b.ins(f"add.rn.f32 {acc[e]}, {acc[e]}, {v[e]};")
+    dst = b.reg("rd")
+    b.ins(f"add.s64 {dst}, {c}, {off};")
+    b.ins(f"st.global.v4.f32 [{dst}], {{{', '.join(acc)}}};")
+    b.ins(f"add.u32 {g}, {g}, {stride};")
+    b.ins(f"bra.uni {top};")
+    b.place(done)
+    return b.render(header=False)
+
+
+def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None, split_k=None):
     """``gather`` > 0: the all-gather variant for a row shard of C.  Instead
     of writing ``C``, the epilogue stores every finished tile into each of
     the up to ``gather`` destinations listed in the module global
@@ -172,6 +270,16 @@ def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None):
     KT = -(-K // BK)
     tiles_m, tiles_n = -(-M // TM), -(-N // BN)
     ntiles = tiles_m * tiles_n
+    # split-K (f32 only, not in the gather variant): SK K slices per tile,
+    # KTS stages each; unit u is tile u % ntiles, slice u // ntiles
+    if split_k is None:
+        split_k = 1 if (lowp or gather) else choose_split_k(ntiles, 148 // CG, K, BK)
+    SK = int(split_k)
+    if SK > 1 and (lowp or gather or KT % SK):
+        raise ValueError(f"split-K {SK} needs an f32 matmul without gather and K/{BK} "
+                         f"divisible by it")
+    KTS = KT // SK
+    nunits = ntiles * SK
     A_STAGE = BM * BK * esz               # 8 KB (tf32) / 16 KB (16-bit)
     B_STAGE = BNC * BK * esz              # 16 KB / 32 KB (BN=256; half that per CTA of a pair)
     if lowp:                              # no split: raw tiles only
@@ -203,6 +311,9 @@ def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None):
         b.module(f".global .align 8 .b8 emmy_gather_dst[{8 * gather}];")
         b.module(".global .align 4 .u32 emmy_gather_n;")
         b.module(".global .align 4 .u32 emmy_gather_row0;")
+    if SK > 1:
+        # the partial tiles' scratch, recorded by the <entry>_part prelaunch
+        b.module(".global .align 8 .u64 emmy_part;")
     b.directive(f".maxntid {T}, 1, 1")
     if pair:
         # launching without the cluster of two fails at launch time
@@ -321,17 +432,27 @@ def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None):
             b.ins(f"add.u32 {r}, {r}, {off};")
         return r
 
+    kslice = {}                          # the current unit's K slice register
+
     def tile_loop(body_fn, label):
-        """for tile = ctaid; tile < ntiles; tile += nctaid: body_fn(tile)"""
-        tile = b.reg("r")
+        """for unit = ctaid; unit < nunits; unit += nctaid: body_fn(tile),
+        with unit = slice * ntiles + tile (split-K) or unit = tile."""
+        unit = b.reg("r")
         top, done = b.label(label), b.label(label + "_END")
         pt = b.reg("p")
-        b.ins(f"mov.u32 {tile}, {cta};")
+        b.ins(f"mov.u32 {unit}, {cta};")
         b.place(top)
-        b.ins(f"setp.ge.u32 {pt}, {tile}, {ntiles};")
+        b.ins(f"setp.ge.u32 {pt}, {unit}, {nunits};")
         b.ins(f"@{pt} bra.uni {done};")
+        if SK > 1:
+            tile, ksl = b.regs("r", 2)
+            b.ins(f"rem.u32 {tile}, {unit}, {ntiles};")
+            b.ins(f"div.u32 {ksl}, {unit}, {ntiles};")
+            kslice["reg"] = ksl
+        else:
+            tile = unit
         body_fn(tile)
-        b.ins(f"add.u32 {tile}, {tile}, {ncta};")
+        b.ins(f"add.u32 {unit}, {unit}, {ncta};")
         b.ins(f"bra.uni {top};")
         b.place(done)
 
@@ -341,7 +462,7 @@ def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None):
         pk = b.reg("p")
         b.ins(f"mov.u32 {ks}, 0;")
         b.place(top)
-        b.ins(f"setp.ge.u32 {pk}, {ks}, {KT};")
+        b.ins(f"setp.ge.u32 {pk}, {ks}, {KTS};")
         b.ins(f"@{pk} bra.uni {done};")
         body_fn(ks)
         b.ins(f"add.u32 {ks}, {ks}, 1;")
@@ -408,7 +529,11 @@ def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None):
                 full = bar_at(FULL, s)
                 tc.arrive_expect_tx(full, nbytes)
             k0 = b.reg("r")
-            b.ins(f"mul.lo.u32 {k0}, {ks}, {BK};")
+            if SK > 1:                      # this unit's K slice
+                b.ins(f"mad.lo.u32 {k0}, {kslice['reg']}, {KTS}, {ks};")
+                b.ins(f"mul.lo.u32 {k0}, {k0}, {BK};")
+            else:
+                b.ins(f"mul.lo.u32 {k0}, {ks}, {BK};")
             for (tma_, tmb_, a_reg, b_reg) in parts:
                 dA = b.reg("r")
                 b.ins(f"mad.lo.u32 {dA}, {s}, {A_STAGE}, {base};")
@@ -546,6 +671,19 @@ def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None):
     b.ins(f"add.u32 {lane_base}, {lane_base}, {tmem};")
     tl_e = b.reg("r")
     b.ins(f"mov.u32 {tl_e}, 0;")
+    if SK > 1:
+        # the _part prelaunch records the scratch for the partial tiles;
+        # without it there is nowhere to write: report and leave (the other
+        # roles' bounded waits then end the kernel)
+        part_base = b.reg("rd")
+        b.ins(f"ld.global.u64 {part_base}, [emmy_part];")
+        pz = b.reg("p")
+        have = b.label("HAVE_PART")
+        b.ins(f"setp.ne.u64 {pz}, {part_base}, 0;")
+        b.ins(f"@{pz} bra.uni {have};")
+        tc.raise_abort(STATUS_NO_PREPASS)
+        b.ins(f"bra.uni {END};")
+        b.place(have)
     if gather:
         gdst = b.regs("rd", gather)
         gn, grow0 = b.regs("r", 2)
@@ -585,7 +723,15 @@ def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None):
         b.ins(f"setp.lt.u32 {prow}, {row}, {M};")
         rowaddr = b.reg("rd")
         b.ins(f"mul.wide.u32 {rowaddr}, {row}, {N * 4};")
-        b.ins(f"add.s64 {rowaddr}, {rowaddr}, {pC};")
+        if SK > 1:
+            # slice s of the tile goes to part[s] (M x N f32 each); the reduce
+            # entry sums the slices into C in slice order
+            po = b.reg("rd")
+            b.ins(f"mul.wide.u32 {po}, {kslice['reg']}, {M * N * 4};")
+            b.ins(f"add.s64 {rowaddr}, {rowaddr}, {po};")
+            b.ins(f"add.s64 {rowaddr}, {rowaddr}, {part_base};")
+        else:
+            b.ins(f"add.s64 {rowaddr}, {rowaddr}, {pC};")
         taddr = b.reg("r")
         b.ins(f"mad.lo.u32 {taddr}, {a}, {BN}, {lane_base};")
         if gather:
@@ -688,7 +834,7 @@ def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None):
 
     sidecar = {
         "category": "matmul",
-        "grid": [CG * min(ntiles, 148 // CG), 1, 1],
+        "grid": [CG * min(nunits, 148 // CG), 1, 1],
         "block": [T, 1, 1],
         "shared_bytes": SMEM,
         "cluster": [CG, 1, 1],
@@ -727,6 +873,16 @@ def emit(comp, plan: MatmulPlan, gather: int = 0, pair=None):
                               {"name": "b_lo", "bytes": K * N * 4}]
         sidecar["prelaunch"] = [split_launch(sa, [plan.a, "@a_lo"], M * K),
                                 split_launch(sb, [plan.b, "@b_lo"], K * N)]
+        if SK > 1:
+            sp, sr = comp.entry + "_part", comp.entry + "_reduce"
+            ptx += "\n" + _emit_record_part(comp.target, comp.ptx_version, sp)
+            ptx += "\n" + _emit_reduce(comp.target, comp.ptx_version, sr, M * N, SK)
+            sidecar["scratch"].append({"name": "c_part", "bytes": SK * M * N * 4})
+            sidecar["prelaunch"].append({"entry": sp, "args": ["@c_part"],
+                                         "grid": [1, 1, 1], "block": [32, 1, 1]})
+            sidecar["postlaunch"] = [split_launch(sr, ["@c_part", plan.c], M * N,
+                                                  max_blocks=148 * 8)]
+        sidecar["split_k"] = SK
     if gather:
         sidecar["gather"] = {"max_destinations": gather, "destinations": "emmy_gather_dst",
                              "count": "emmy_gather_n", "row0": "emmy_gather_row0",

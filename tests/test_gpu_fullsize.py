@@ -133,3 +133,35 @@ def test_full_size_kernel_matches_reference_ptx_and_float64(cuda, tag):
     print(tag, "; ".join(report))
     del want, got, x
     torch.cuda.empty_cache()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,split", [(2048, 2)])
+def test_matmul_shard_with_split_k_matches_float64(cuda, rows, split):
+    """The row shard of the 8192^3 matmul at 4 ranks (2048 rows of C) is cut
+    along K (its pair tiles alone fill 3.46 waves of the 74 CTA pairs); the
+    partial tiles, summed by the reduce entry, give C within the matmul
+    tolerance of float64, and twice in a row the same bits."""
+    import torch
+    from emmy_ptx import workloads
+    from emmy_ptx.runtime import Kernel
+    p = workloads.build("matmul", m=rows, n=8192, k=8192)
+    host = p.make_inputs()
+    x = {n: torch.from_numpy(a).to(cuda) for n, a in host.items()}
+    del host
+    with tempfile.TemporaryDirectory() as td:
+        kern = Kernel.from_ir(p.write(td))
+    assert kern.sidecar["split_k"] == split and kern.sidecar["postlaunch"]
+    got = _outputs(torch, p, cuda)
+    launch = kern.bind({**x, **got})
+    launch()
+    torch.cuda.synchronize()
+    first = got["C"].clone()
+    launch()
+    torch.cuda.synchronize()
+    assert kern.status() == 0
+    assert torch.equal(first, got["C"]), "split-K sums are not deterministic"
+    want = x["A"].double() @ x["B"].double()
+    ok, msg = check_close_device("matmul", "C vs float64", got["C"], want, x)
+    assert ok, msg
+    kern.free_scratch()

@@ -162,3 +162,27 @@ def test_misaligned_argument_is_refused_before_launch(cuda):
     with pytest.raises(EmmyRuntimeError, match="aligned"):
         kern.bind({"x": x[1:n + 1], "y": y, "out": out})
     assert kern.launches == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("split", [2, 4])
+def test_split_k_matmul_matches_oracle(cuda, split):
+    """A split-K matmul (forced on a small shape): K slices accumulate into
+    their own partial tiles, the reduce entry sums them in slice order."""
+    from emmy_ptx import workloads
+    from emmy_ptx.compiler import Compiler
+    from emmy_ptx.runtime import Kernel
+    from emmy_ptx.sm100 import matmul
+    p = workloads.build("matmul", m=256, n=256, k=1024)
+    inputs = p.make_inputs()
+    with tempfile.TemporaryDirectory() as td:
+        ir_path = p.write(td)
+        comp = Compiler(ir_path, target="sm_100a", ptx_version="8.8")
+        ptx, side = matmul.emit(comp, matmul.match(comp), split_k=split)
+        assert side["split_k"] == split
+        geom = {"grid": comp.kmeta.get("grid") or [1], "block": comp.kmeta.get("block") or [1]}
+        kern = Kernel(ptx, comp.entry, Kernel._arg_specs(comp), geom, side)
+        got = run_on_gpu(kern, p, inputs, cuda)
+        want = _oracle(p, ir_path, inputs)
+    ok, msg = check_close(p.category, "C", got["C"], want["C"], inputs)
+    assert ok, msg

@@ -233,3 +233,43 @@ def test_attention_with_one_head_group_keeps_the_whole_pre_pass(tmp_path):
     ptx, side = attention.emit(comp, attention.match(comp))
     assert side["inline_split"] is None and side["register_split"] is None
     assert side["block"] == [256, 1, 1] and "setmaxnreg" not in ptx
+
+
+def test_split_k_is_chosen_for_shards_that_fill_the_gpu_badly():
+    """256 pair tiles on 74 CTA pairs are 3.46 waves (0.865 busy); two K
+    slices make 6.92 waves (0.988).  The full 8192^3 (1024 tiles), a
+    4096-row shard (512 tiles) and a 1024-row one (128 tiles; two slices
+    would not fill the last wave better) stay whole."""
+    from emmy_ptx.sm100 import matmul
+    assert matmul.choose_split_k(128, 74, 8192, 16) == 1
+    assert matmul.choose_split_k(256, 74, 8192, 16) == 2
+    assert matmul.choose_split_k(512, 74, 8192, 16) == 1
+    assert matmul.choose_split_k(1024, 74, 8192, 16) == 1
+    assert matmul.choose_split_k(128, 74, 2048, 16) == 1      # slices would be too short
+    assert abs(matmul.wave_efficiency(512, 74) - 512 / 518) < 1e-12
+
+
+def test_split_k_kernel_writes_partials_and_a_reduce_entry(tmp_path):
+    from emmy_ptx import workloads
+    from emmy_ptx.sm100 import matmul
+    p = workloads.build("matmul", m=2048, n=8192, k=8192)
+    comp = Compiler(p.write(tmp_path), target="sm_100a", ptx_version="8.8")
+    ptx, side = matmul.emit(comp, matmul.match(comp))
+    assert side["split_k"] == 2
+    assert {"name": "c_part", "bytes": 2 * 2048 * 8192 * 4} in side["scratch"]
+    assert side["prelaunch"][-1] == {"entry": "k_matmul_f32_part", "args": ["@c_part"],
+                                     "grid": [1, 1, 1], "block": [32, 1, 1]}
+    (post,) = side["postlaunch"]
+    assert post["entry"] == "k_matmul_f32_reduce" and post["args"] == ["@c_part", "C"]
+    red = ptx.split(".visible .entry k_matmul_f32_reduce(")[1]
+    assert red.count("add.rn.f32") == 4 * 1                    # one add per value
+    assert ".visible .entry k_matmul_f32_part(" in ptx and "emmy_part" in ptx
+    report = _build.ptxas_check(ptx)
+    assert "0 bytes spill stores" in report, report
+    # the whole problem, and the gather variant, stay unsplit
+    full = workloads.build("matmul", m=8192, n=8192, k=8192)
+    comp = Compiler(full.write(tmp_path / "full"), target="sm_100a", ptx_version="8.8")
+    assert matmul.emit(comp, matmul.match(comp))[1]["split_k"] == 1
+    comp = Compiler(p.write(tmp_path / "g"), target="sm_100a", ptx_version="8.8")
+    ptx, side = matmul.emit(comp, matmul.match(comp), gather=8)
+    assert side["split_k"] == 1 and "postlaunch" not in side
