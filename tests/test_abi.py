@@ -72,3 +72,27 @@ def test_required_alignment_follows_the_widest_vector_access():
     assert rt.required_alignment(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%r1], [%rd1], 16, [%r2];"
     ) == 16
+
+
+def test_register_split_is_checked_against_the_loaded_function():
+    """A kernel whose warpgroups re-divide registers (setmaxnreg) is refused
+    when the loaded function has fewer registers per thread than the split
+    assumes -- setmaxnreg.inc would wait forever -- and accepted otherwise."""
+    class FakeModule:
+        def __init__(self, regs):
+            self.regs = regs
+
+        def attrs(self, entry):
+            return {"num_regs": self.regs}
+
+    side = {"register_split": {"launch": 168, "registers_by_block": {
+        "288": 128 * (224 + 96) + 32 * 168, "256": 128 * (224 + 96)}}}
+    k = rt.Kernel.__new__(rt.Kernel)
+    k.entry, k.sidecar = "k_attention_causal", side
+    k.module = FakeModule(168)
+    k._check_register_split()                   # fits
+    k.module = FakeModule(160)
+    with pytest.raises(rt.EmmyRuntimeError, match="registers"):
+        k._check_register_split()
+    k.sidecar = {}
+    k._check_register_split()                   # nothing to check
