@@ -25,11 +25,11 @@ the others:
   head, so doing this in the attention kernel would repeat the work S/128
   times; the tensor core drops the low 13 bits of an f32 operand, so an
   unrounded V would bias every product towards zero).  With more than one
-  head group the pre-pass covers group 0 only, and warp 8 of the kernel
-  writes the later groups while the other warps compute: it takes chunks
+  head group the pre-pass covers group 0 only, and warps 8 and 9 of the
+  kernel write the later groups while the other warps compute: it takes chunks
   (up to 128 per group) from a counter in global memory and releases each
   on its group's count, which the producers acquire before their first
-  load of a group's K lo / rounded V.  The 288-thread launch has 168
+  load of a group's K lo / rounded V.  The 320-thread launch has 168
   registers per thread; warps 0-3 raise theirs to 224 and warps 4-7 lower
   theirs to 96 (``setmaxnreg``).  On a 256-thread launch (the meta.json
   block) every warp splits first and then takes its role.
@@ -91,19 +91,21 @@ ROLE_SOFTMAX, ROLE_PRODUCER, ROLE_MMA = 5, 6, 7
 # ready, Q ready): 4 = one per warp, 128 = one per thread
 ARRIVALS = 4
 # K's lo part and the rounded V of every head group but the first are
-# written inside the kernel, by a ninth warp that takes chunks of the work
+# written inside the kernel, by split warps (8 and 9) that take chunks of the work
 # from a shared counter while the other warps compute; the pre-pass then
 # covers group 0 only.  (CTA pairs keep the whole pre-pass.)
 INLINE_SPLIT = True
 SPLIT_CHUNKS = 128         # chunks per head group, at most
 ROLE_SPLIT = 8
-# With nine warps one SM sub-partition holds three of them, so ptxas gives
+# With nine or ten warps an SM sub-partition holds three, so ptxas gives
 # each thread at most 168 registers at launch.  The warpgroups then re-divide
 # them (setmaxnreg): the softmax warps take REG_SOFTMAX, the producer / MMA
-# warps keep REG_ISSUE, the split warp keeps the launch count.  The shares
+# warps lower theirs to REG_ISSUE, the split warps keep the launch count.  The shares
 # must fit the launch's registers (checked against ptxas's count).
 REG_LAUNCH, REG_SOFTMAX, REG_ISSUE = 168, 224, 96
-assert 128 * (REG_SOFTMAX + REG_ISSUE) + 32 * REG_LAUNCH <= 288 * REG_LAUNCH
+SPLIT_WARPS = 2            # split warps per CTA (warps 8 and 9; one measured 0.8% slower)
+assert 128 * (REG_SOFTMAX + REG_ISSUE) + 32 * SPLIT_WARPS * REG_LAUNCH <= \
+    (256 + 32 * SPLIT_WARPS) * REG_LAUNCH
 assert 128 * (REG_SOFTMAX + REG_ISSUE) <= 256 * REG_LAUNCH     # the 256-thread launch
 
 
@@ -372,7 +374,8 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     inline = INLINE_SPLIT and not pair and NG > 1 and CH > 0
     CHV = nvg // CH if inline else 0   # vectors per chunk
     SUN = max(u for u in (1, 2, 4) if (CHV // 32) % u == 0) if inline else 1
-    TL = T + 32 if inline else T       # launch block: the split warp is warp 8
+    SW = SPLIT_WARPS if inline else 0
+    TL = T + 32 * SW                   # launch block: the split warps are warps 8 ...
     DC = D // 32                       # 32-dim chunks
     nqt = -(-S // BQ)
     nqu = -(-nqt // CG)                # query units: tiles, or pairs of tiles
@@ -683,14 +686,14 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
              b.label("MMA_PV")]
     pr = b.reg("p")
     if inline:
-        # warp 8 splits; a launch without it (the meta.json block of 256
-        # threads) has every warp split first, then take its role
+        # warps 8 and 9 split; a launch without them (the meta.json block of
+        # 256 threads) has every warp split first, then take its role
         pall, nth = b.reg("p"), b.reg("r")
         SPLIT, DISPATCH = b.label("SPLIT"), b.label("DISPATCH")
         b.ins(f"mov.u32 {nth}, %ntid.x;")
         b.ins(f"setp.lt.u32 {pall}, {nth}, {TL};")
         b.ins(f"@{pall} bra.uni {SPLIT};")
-        b.ins(f"setp.eq.u32 {pr}, {warp}, 8;")
+        b.ins(f"setp.ge.u32 {pr}, {warp}, 8;")
         b.ins(f"@{pr} bra.uni {SPLIT};")
         b.place(DISPATCH)
     if inline:
@@ -1600,13 +1603,14 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         "prelaunch": [split_launch(split_entry, [plan.k, plan.v, "@k_lo", "@v_r"],
                                    pre_elems, max_blocks=148 * 16,
                                    vec=8 if wide_vectors(comp.ptx_version) else 4)],
-        "inline_split": {"groups": NG, "chunks_per_group": CH, "warp": 8} if inline else None,
+        "inline_split": {"groups": NG, "chunks_per_group": CH,
+                         "warps": list(range(8, 8 + SW))} if inline else None,
         # setmaxnreg shares: registers per thread at launch, and the total the
         # warpgroups hold after the split, for the tuned block and the
         # meta.json one (the runtime refuses a build with fewer at launch)
         "register_split": {"launch": REG_LAUNCH, "softmax": REG_SOFTMAX, "issue": REG_ISSUE,
                            "registers_by_block": {
-                               str(TL): 128 * (REG_SOFTMAX + REG_ISSUE) + 32 * REG_LAUNCH,
+                               str(TL): 128 * (REG_SOFTMAX + REG_ISSUE) + 32 * SW * REG_LAUNCH,
                                str(T): 128 * (REG_SOFTMAX + REG_ISSUE)}} if inline else None,
         "tensormaps": [tmap("tmap_Khi", plan.k, "128B"),     # K itself: hi = K, low bits dropped
                        tmap("tmap_Klo", "@k_lo", "128B"),

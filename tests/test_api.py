@@ -151,6 +151,6 @@ def test_every_config_has_an_sm100a_lowering(name, tmp_path):
     # the kernel keeps the meta.json block size; attention with several head
     # groups adds its split warp to the tuned launch and still runs (split
     # first, then compute) on the meta.json block
-    extra = 32 if side.get("inline_split") else 0
+    extra = 32 * len(side["inline_split"]["warps"]) if side.get("inline_split") else 0
     assert side["block"][0] == p.block[0] + extra, "the kernel keeps the meta.json block size"
     assert side["arg_order"] == p.inputs + p.outputs
