@@ -25,11 +25,11 @@ the others:
   head, so doing this in the attention kernel would repeat the work S/128
   times; the tensor core drops the low 13 bits of an f32 operand, so an
   unrounded V would bias every product towards zero).  With more than one
-  head group the pre-pass covers group 0 only, and warps 8 and 9 of the
+  head group the pre-pass covers group 0 only, and warps 8-11 of the
   kernel write the later groups while the other warps compute: it takes chunks
   (up to 128 per group) from a counter in global memory and releases each
   on its group's count, which the producers acquire before their first
-  load of a group's K lo / rounded V.  The 320-thread launch has 168
+  load of a group's K lo / rounded V.  The 384-thread launch has 168
   registers per thread; warps 0-3 raise theirs to 224 and warps 4-7 lower
   theirs to 96 (``setmaxnreg``).  On a 256-thread launch (the meta.json
   block) every warp splits first and then takes its role.
@@ -91,19 +91,21 @@ ROLE_SOFTMAX, ROLE_PRODUCER, ROLE_MMA = 5, 6, 7
 # ready, Q ready): 4 = one per warp, 128 = one per thread
 ARRIVALS = 4
 # K's lo part and the rounded V of every head group but the first are
-# written inside the kernel, by split warps (8 and 9) that take chunks of the work
+# written inside the kernel, by split warps (8-11) that take chunks of the work
 # from a shared counter while the other warps compute; the pre-pass then
 # covers group 0 only.  (CTA pairs keep the whole pre-pass.)
 INLINE_SPLIT = True
 SPLIT_CHUNKS = 128         # chunks per head group, at most
 ROLE_SPLIT = 8
-# With nine or ten warps an SM sub-partition holds three, so ptxas gives
+# With nine to twelve warps an SM sub-partition holds three, so ptxas gives
 # each thread at most 168 registers at launch.  The warpgroups then re-divide
 # them (setmaxnreg): the softmax warps take REG_SOFTMAX, the producer / MMA
 # warps lower theirs to REG_ISSUE, the split warps keep the launch count.  The shares
 # must fit the launch's registers (checked against ptxas's count).
 REG_LAUNCH, REG_SOFTMAX, REG_ISSUE = 168, 224, 96
-SPLIT_WARPS = 2            # split warps per CTA (warps 8 and 9; one measured 0.8% slower)
+# split warps per CTA (warps 8-11, one warpgroup): against one, two measured 0.03 ms and
+# four another 0.05 ms faster (alternating pairs); more would cut the launch below 168
+SPLIT_WARPS = 4
 assert 128 * (REG_SOFTMAX + REG_ISSUE) + 32 * SPLIT_WARPS * REG_LAUNCH <= \
     (256 + 32 * SPLIT_WARPS) * REG_LAUNCH
 assert 128 * (REG_SOFTMAX + REG_ISSUE) <= 256 * REG_LAUNCH     # the 256-thread launch
@@ -686,7 +688,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
              b.label("MMA_PV")]
     pr = b.reg("p")
     if inline:
-        # warps 8 and 9 split; a launch without them (the meta.json block of
+        # warps 8-11 split; a launch without them (the meta.json block of
         # 256 threads) has every warp split first, then take its role
         pall, nth = b.reg("p"), b.reg("r")
         SPLIT, DISPATCH = b.label("SPLIT"), b.label("DISPATCH")

@@ -86,7 +86,7 @@ def test_register_split_is_checked_against_the_loaded_function():
             return {"num_regs": self.regs}
 
     side = {"register_split": {"launch": 168, "registers_by_block": {
-        "320": 128 * (224 + 96) + 64 * 168, "256": 128 * (224 + 96)}}}
+        "384": 128 * (224 + 96) + 128 * 168, "256": 128 * (224 + 96)}}}
     k = rt.Kernel.__new__(rt.Kernel)
     k.entry, k.sidecar = "k_attention_causal", side
     k.module = FakeModule(168)

@@ -192,24 +192,25 @@ def test_row_gather_variant_stores_to_every_destination(tmp_path, name, kw):
     (dict(batch=8, heads=32, seq=4096, head_dim=128), 32, 128)])
 def test_attention_splits_head_groups_in_the_kernel(tmp_path, kw, groups, chunks):
     """With several head groups the pre-pass covers group 0 and prepares the
-    split state; warps 8 and 9 take chunks of the later groups from a shared
+    split state; warps 8-11 take chunks of the later groups from a shared
     counter and releases each on its group's count, which the producers
     acquire (bounded) before their TMA loads.  The warpgroups re-divide the
-    168 registers per thread of the 320-thread launch with setmaxnreg, and the
+    168 registers per thread of the 384-thread launch with setmaxnreg, and the
     shares fit both the tuned block and the meta.json block of 256."""
     from emmy_ptx import workloads
     from emmy_ptx.sm100 import attention
     p = workloads.attention(causal=True, **kw)
     comp = Compiler(p.write(tmp_path), target="sm_100a", ptx_version="8.8")
     ptx, side = attention.emit(comp, attention.match(comp))
-    assert side["inline_split"] == {"groups": groups, "chunks_per_group": chunks, "warps": [8, 9]}
-    assert side["block"] == [320, 1, 1]
+    assert side["inline_split"] == {"groups": groups, "chunks_per_group": chunks,
+                                    "warps": [8, 9, 10, 11]}
+    assert side["block"] == [384, 1, 1]
     rs = side["register_split"]
     assert rs["launch"] == 168
     for threads, need in rs["registers_by_block"].items():
         assert need <= int(threads) * rs["launch"]
     main, pre = ptx.split(".visible .entry k_attention_causal_ksplit(")
-    assert ".maxntid 320, 1, 1" in main and ".maxnreg 168" in main
+    assert ".maxntid 384, 1, 1" in main and ".maxnreg 168" in main
     assert main.count("setmaxnreg.inc.sync.aligned.u32 224;") == 1
     assert main.count("setmaxnreg.dec.sync.aligned.u32 96;") == 1
     assert main.count("atom.global.add.u32") == 1
