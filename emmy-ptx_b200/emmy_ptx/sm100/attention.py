@@ -106,6 +106,9 @@ REG_LAUNCH, REG_SOFTMAX, REG_ISSUE = 168, 224, 96
 # split warps per CTA (warps 8-11, one warpgroup): against one, two measured 0.03 ms and
 # four another 0.05 ms faster (alternating pairs); more would cut the launch below 168
 SPLIT_WARPS = 4
+# vectors of K and of V per lane in flight (the largest that divides); 8 measured
+# 0.12 ms slower than 4 (alternating pairs)
+SPLIT_UNROLLS = (1, 2, 4)
 assert 128 * (REG_SOFTMAX + REG_ISSUE) + 32 * SPLIT_WARPS * REG_LAUNCH <= \
     (256 + 32 * SPLIT_WARPS) * REG_LAUNCH
 assert 128 * (REG_SOFTMAX + REG_ISSUE) <= 256 * REG_LAUNCH     # the 256-thread launch
@@ -375,7 +378,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     CH = max([c for c in range(1, SPLIT_CHUNKS + 1) if nvg % (32 * c) == 0] or [0])
     inline = INLINE_SPLIT and not pair and NG > 1 and CH > 0
     CHV = nvg // CH if inline else 0   # vectors per chunk
-    SUN = max(u for u in (1, 2, 4) if (CHV // 32) % u == 0) if inline else 1
+    SUN = max(u for u in SPLIT_UNROLLS if (CHV // 32) % u == 0) if inline else 1
     SW = SPLIT_WARPS if inline else 0
     TL = T + 32 * SW                   # launch block: the split warps are warps 8 ...
     DC = D // 32                       # 32-dim chunks
