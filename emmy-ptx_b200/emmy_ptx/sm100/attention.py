@@ -96,6 +96,7 @@ ARRIVALS = 4
 # covers group 0 only.  (CTA pairs keep the whole pre-pass.)
 INLINE_SPLIT = True
 SPLIT_CHUNKS = 128         # chunks per head group, at most
+PREPASS_GROUPS = 1         # head groups the pre-pass covers (2 measured within noise: +0.4%)
 ROLE_SPLIT = 8
 # With nine to twelve warps an SM sub-partition holds three, so ptxas gives
 # each thread at most 168 registers at launch.  The warpgroups then re-divide
@@ -218,12 +219,13 @@ def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: 
     vectors and 16 blocks per SM the full-size pass (2 GB) measured 0.332
     ms against 0.368 with 16-byte vectors and 8 blocks per SM.
 
-    ``split_groups = (groups, chunks)``: the attention kernel splits every
-    head group but the first itself (``emit``, the split warp), and this
-    entry covers group 0 only (``n_elems`` = its elements).  Its thread 0
-    also prepares the kernel's split state in the module globals: the
-    ``k_lo`` / ``v_r`` addresses, the chunk counter at zero, and the
-    per-group chunks-done counts (group 0 complete, the others zero)."""
+    ``split_groups = (groups, chunks, covered)``: the attention kernel
+    splits every head group from ``covered`` on itself (``emit``, the split
+    warps), and this entry covers the first ``covered`` groups (``n_elems``
+    = their elements).  Its thread 0 also prepares the kernel's split state
+    in the module globals: the ``k_lo`` / ``v_r`` addresses, the chunk
+    counter at zero, and the per-group chunks-done counts (the covered
+    groups complete, the others zero)."""
     vw = 8 if wide_vectors(version) else 4
     assert n_elems % vw == 0
     b = KernelBuilder(entry, target, version)
@@ -243,7 +245,7 @@ def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: 
     b.ins(f"mul.lo.u32 {stride}, {stride}, {nt};")
     b.ins(f"mov.u32 {t}, %tid.x;")
     if split_groups is not None:
-        ngroups, nchunks = split_groups
+        ngroups, nchunks, covered = split_groups
         p0 = b.reg("p")
         b.ins(f"or.b32 {g}, {g}, {t};")
         b.ins(f"setp.ne.u32 {p0}, {g}, 0;")
@@ -259,15 +261,17 @@ def emit_kv_prepass(target: str, version: str, entry: str, n_elems: int, block: 
         b.ins(f"mov.u64 {ga}, emmy_split_next;")
         b.ins(f"st.global.u32 [{ga}], {zero};")
         b.ins(f"mov.u64 {ga}, emmy_split_done;")
-        b.ins(f"st.global.u32 [{ga}], {full};")
-        i, pi = b.reg("r"), b.reg("p")
+        i, pi, v_ = b.reg("r"), b.reg("p"), b.reg("r")
         loop, ldone = b.label("SPLIT_ZERO"), b.label("SPLIT_ZERO_END")
-        b.ins(f"mov.u32 {i}, 1;")
+        b.ins(f"mov.u32 {i}, 0;")
         b.place(loop)
         b.ins(f"setp.ge.u32 {pi}, {i}, {ngroups};")
         b.ins(f"@{pi} bra {ldone};")
+        # the groups this pre-pass covers are complete, the others not begun
+        b.ins(f"setp.lt.u32 {pi}, {i}, {covered};")
+        b.ins(f"selp.b32 {v_}, {full}, {zero}, {pi};")
+        b.ins(f"st.global.u32 [{ga}], {v_};")
         b.ins(f"add.s64 {ga}, {ga}, 4;")
-        b.ins(f"st.global.u32 [{ga}], {zero};")
         b.ins(f"add.u32 {i}, {i}, 1;")
         b.ins(f"bra {loop};")
         b.place(ldone)
@@ -376,7 +380,8 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     SVW = 8 if wide_vectors(comp.ptx_version) else 4
     nvg = G * S * D // SVW             # vectors per head group
     CH = max([c for c in range(1, SPLIT_CHUNKS + 1) if nvg % (32 * c) == 0] or [0])
-    inline = INLINE_SPLIT and not pair and NG > 1 and CH > 0
+    PG = PREPASS_GROUPS                # head groups the pre-pass covers
+    inline = INLINE_SPLIT and not pair and NG > PG and CH > 0
     CHV = nvg // CH if inline else 0   # vectors per chunk
     SUN = max(u for u in SPLIT_UNROLLS if (CHV // 32) % u == 0) if inline else 1
     SW = SPLIT_WARPS if inline else 0
@@ -761,10 +766,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
         b.ins(f"@{pl0} atom.global.add.u32 {c}, [{nxt}], 1;")
         b.ins(f"shfl.sync.idx.b32 {c}, {c}, 0, 0x1f, 0xffffffff;")
         pc = b.reg("p")
-        b.ins(f"setp.ge.u32 {pc}, {c}, {(NG - 1) * CH};")
+        b.ins(f"setp.ge.u32 {pc}, {c}, {(NG - PG) * CH};")
         b.ins(f"@{pc} bra.uni {send};")
-        cg = b.reg("r")                    # chunk index counting group 0's
-        b.ins(f"add.u32 {cg}, {c}, {CH};")
+        cg = b.reg("r")                    # chunk index counting the pre-pass groups
+        b.ins(f"add.u32 {cg}, {c}, {PG * CH};")
         grp = b.reg("r")
         b.ins(f"div.u32 {grp}, {cg}, {CH};")
         off = b.reg("rd")
@@ -1580,10 +1585,10 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     tc.tmem_dealloc(tmem, TMEM_COLS)
     b.place(fin)
 
-    pre_elems = G * S * D if inline else B * H * S * D
+    pre_elems = PG * G * S * D if inline else B * H * S * D
     ptx = b.render() + "\n" + emit_kv_prepass(comp.target, comp.ptx_version, split_entry,
                                               pre_elems,
-                                              split_groups=(NG, CH) if inline else None)
+                                              split_groups=(NG, CH, PG) if inline else None)
 
     pairs = B * H * (S * (S + 1) // 2 if plan.causal else S * S)
     kv_tiles = 0                      # (128-query tile, 128-key tile) products issued
