@@ -376,7 +376,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     G = head_group(B * H)
     NG = B * H // G                    # head groups
     # in-kernel split: chunks of a head group, each a whole number of the
-    # split warp's 32-lane vector rows
+    # split warps' 32-lane vector rows
     SVW = 8 if wide_vectors(comp.ptx_version) else 4
     nvg = G * S * D // SVW             # vectors per head group
     CH = max([c for c in range(1, SPLIT_CHUNKS + 1) if nvg % (32 * c) == 0] or [0])
@@ -729,7 +729,7 @@ def emit(comp, plan: AttnPlan, gather: int = 0, pair=None):
     b.ins(f"bra.uni {roles[4]};")              # warp 7
 
     if inline:
-        # ---- split warp: K's lo part and the rounded V of groups 1.. ---------
+        # ---- split warps: K's lo part and the rounded V of groups 1.. --------
         # Chunk c (groups 1.. in order, CH chunks each) is taken from the
         # shared counter, so the resident warps share the work whatever the
         # grid; a chunk's completion is released on its group's counter,
